@@ -1,0 +1,178 @@
+/*
+ * bna_b200.h — C ABI of the B200-native compressed Butterfly attention library
+ * (libbna_b200.so).  Plain C: raw pointers, integer sizes/strides, a cudaStream_t
+ * passed as void*.  No PyTorch types cross this boundary.
+ *
+ * Every entry point returns a bna_status; on failure bna_last_error() returns a
+ * thread-local message.  The caller owns every buffer (inputs, outputs, cache pools);
+ * the library never allocates or frees device memory.  All work is enqueued on the
+ * given stream; nothing synchronises the host except the *_host selection dumps.
+ *
+ * Reference interfaces replaced (paths inside the Hmbown/Butterfly project):
+ *   bna/torch/attention_wayfinder_permute.py  build_block_butterfly_layout      :568-682
+ *   bna/torch/attention_wayfinder_permute.py  _compressed_butterfly_block_index_tensors :912-966
+ *   bna/torch/attention_wayfinder_permute.py  _compressed_butterfly_active_index_tensors :969-1019
+ *   bna/torch/attention_wayfinder_permute.py  _block_mean_summaries_torch       :1022-1043
+ *   bna/torch/attention_wayfinder_permute.py  butterfly_compressed_attention    :1046-1122
+ *   bna/torch/attention_wayfinder_permute.py  butterfly_compressed_attention_active :1125-1197
+ *   bna/mlx/compressed_cache.py               CompressedKVCache.update_and_fetch :94-172
+ *   bna/mlx/attention.py                      compressed_butterfly_attention_from_cache :1816-1876
+ */
+#ifndef BNA_B200_H
+#define BNA_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BNA_API __attribute__((visibility("default")))
+#else
+#define BNA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  BNA_OK = 0,
+  BNA_BAD_SHAPE = 1,      /* shape/size mismatch or non-positive size  (reference: ValueError) */
+  BNA_BAD_STRIDE = 2,     /* stride/alignment not usable (innermost dim must be contiguous)   */
+  BNA_BAD_DTYPE = 3,      /* dtype not supported on this path                                 */
+  BNA_CAPACITY = 4,       /* cache tail / summary capacity exceeded (reference: RuntimeError)  */
+  BNA_UNSUPPORTED = 5,    /* configuration outside what the kernels implement                  */
+  BNA_CUDA_ERROR = 6,     /* a CUDA runtime/driver call failed                                 */
+  BNA_DEVICE_TIMEOUT = 7  /* a kernel gave up a bounded wait and returned early               */
+} bna_status;
+
+typedef enum { BNA_BF16 = 0, BNA_F16 = 1 } bna_dtype;
+
+/* Partner rules of bna/topology/butterfly.py:108-141 used by the block-sparse layout. */
+typedef enum {
+  BNA_RULE_CAUSAL_SHIFT = 0,
+  BNA_RULE_XOR = 1,
+  BNA_RULE_BIT_REVERSAL = 2,
+  BNA_RULE_BENES = 3
+} bna_rule;
+
+/* A strided 4-D view [d0, d1, d2, d3] with element strides; d3 (head_dim) must have
+ * stride 1.  Used for q/k/v [B, H, T, dh], outputs and cache pools. */
+typedef struct {
+  void* data;
+  int64_t size[4];
+  int64_t stride[4];
+} bna_tensor4;
+
+/* Block routing of one layer (replaces BlockHamiltonianLayout, :382-405).
+ * If `neighbors` is non-NULL it is a DEVICE int32 table [num_blocks, max_degree]
+ * (-1 padded, head 0 rows of block_neighbors) and the rule fields are ignored;
+ * otherwise rows are generated in closed form from the rule fields. */
+typedef struct {
+  int32_t block_size;
+  int32_t num_blocks;
+  int32_t max_degree;          /* summary slots per row (>= 1, <= 16) */
+  int32_t rule;                /* bna_rule */
+  int32_t width;               /* ceil(log2(num_blocks)), 1 if num_blocks <= 1 */
+  int32_t stage_idx;
+  int32_t stage_count;
+  int32_t partner_count;       /* <= 8 */
+  int32_t local_window_blocks;
+  int32_t sink_count;
+  const int32_t* neighbors;    /* optional device table */
+} bna_route;
+
+BNA_API const char* bna_last_error(void);
+BNA_API const char* bna_version(void);
+
+/* Reads and clears the device-side error word set by kernels that gave up a bounded
+ * wait (0 = none).  Synchronises the given device. */
+BNA_API int bna_take_device_error(int device, int32_t* code_out);
+
+/* ---- topology / selection (host) -------------------------------------------------- */
+
+/* Fill `route` (everything but `neighbors`) for a layer; replaces
+ * build_block_butterfly_layout's metadata (:568-682, butterfly.py:52-105). */
+BNA_API int bna_route_init(bna_route* route, int32_t seq_len, int32_t block_size, int32_t layer_idx,
+                   int32_t local_window_blocks, int32_t sink_count, int32_t partner_count,
+                   int32_t rule);
+
+/* Host dump of the block_neighbors rows [num_blocks, max_degree] (-1 padded). */
+BNA_API int bna_block_neighbors_host(const bna_route* route, int32_t* out);
+
+/* Host dump of prefill selection (:912-966): per block the raw-window start and the
+ * cursor-packed valid summary blocks ([num_blocks, max_degree], -1 padded) and count.
+ * Uses the same selection code the kernels run.  route->neighbors must be NULL or
+ * a HOST table for this call. */
+BNA_API int bna_prefill_selection_host(const bna_route* route, int32_t seq_len, int32_t window,
+                               int32_t* local_start, int32_t* summary_idx, int32_t* summary_count);
+
+/* Host dump of active-row selection (:969-1019) for `n` query positions. */
+BNA_API int bna_active_selection_host(const bna_route* route, int32_t window, const int64_t* positions,
+                              int32_t n, int32_t num_summary_limit, int32_t* block,
+                              int32_t* local_start, int32_t* summary_idx, int32_t* summary_count);
+
+/* Device dump of the same selections, computed by the device code path (for parity). */
+BNA_API int bna_prefill_selection_device(const bna_route* route, int32_t seq_len, int32_t window,
+                                 int32_t* summary_idx, int32_t* summary_count, void* stream);
+
+/* ---- K1: mean-pool block compressor (:1022-1043; cache close :133-140) -------------- */
+
+/* out[b,h,slot0+j,:] = mean of the valid tokens of block j (j < n_blocks) of x, where
+ * block j covers positions [pos0 + j*block_size, ...) clipped to `valid_len` positions
+ * counted from pos0 (partial last block averaged over its valid tokens, >= 1).
+ * Token position p is read at x[b,h,idx,:] with idx = p % ring (ring > 0) or
+ * idx = p - pos0 (ring == 0).  fp32 accumulation, rounded store in x's dtype. */
+BNA_API int bna_compress_blocks(const bna_tensor4* x, bna_tensor4* out, int32_t dtype, int32_t block_size,
+                        int64_t pos0, int32_t n_blocks, int64_t valid_len, int64_t ring,
+                        int64_t slot0, void* stream);
+
+/* ---- K2: prefill attention on tcgen05/TMEM (:1046-1122) -------------------------------
+ * q [B,Hq,Tq,dh] (any strides, dh contiguous, 16-byte aligned rows), k/v [B,Hkv,Tk,dh],
+ * k_sum/v_sum [B,Hkv,N,dh] block means, out [B,Hq,Tq,dh] (same dtype), lse (optional,
+ * fp32, element strides lse_stride_b/h, token-contiguous).
+ * Query row i has global position q_pos0+i; key row j has global position kv_pos0+j;
+ * selection uses `route` over a sequence of total_len tokens.  dh must be 128,
+ * Hq/Hkv in {1,2,4,8}.  scale = softmax scale (1/sqrt(dh) for SDPA's default). */
+BNA_API int bna_prefill_attention(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4* v,
+                          const bna_tensor4* k_sum, const bna_tensor4* v_sum, bna_tensor4* out,
+                          float* lse, int64_t lse_stride_b, int64_t lse_stride_h, int32_t dtype,
+                          const bna_route* route, int32_t window, int64_t q_pos0, int64_t kv_pos0,
+                          int64_t total_len, float scale, void* stream);
+
+/* ---- K4: active / decode attention (:1125-1197; MLX from_cache :1669-1876) -------------
+ * One query row per (b, query index).  Raw keys for position p are the positions
+ * [max(0,p-W+1), p]; position x is read at k[b,h,x % ring] (ring > 0) or
+ * k[b,h,x - kv_pos0] (ring == 0).  Summaries are read at k_sum[b,h,n].  Query positions
+ * come from `positions` (device int64, length Tq) or, if NULL, pos0 + index.
+ * num_summary_limit bounds usable summary blocks (summary_count of a cache).
+ * Selection block = min(p / block_size, route->num_blocks - 1). */
+BNA_API int bna_active_attention(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4* v,
+                         const bna_tensor4* k_sum, const bna_tensor4* v_sum, bna_tensor4* out,
+                         float* lse, int64_t lse_stride_b, int64_t lse_stride_h, int32_t dtype,
+                         const bna_route* route, int32_t window, const int64_t* positions,
+                         int64_t pos0, int64_t kv_pos0, int64_t ring, int32_t num_summary_limit,
+                         float scale, void* stream);
+
+/* ---- K3: two-pool cache (bna/mlx/compressed_cache.py:94-172) --------------------------
+ * Ring tail [B,Hkv,ring,dh] and summary pool [B,Hkv,capacity,dh].  Counter logic lives
+ * in the host (it is pure integer bookkeeping); these move the data. */
+
+/* Write src [B,Hkv,step,dh] at positions pos0..pos0+step-1 into ring slots p % ring. */
+BNA_API int bna_cache_append(bna_tensor4* ring_k, bna_tensor4* ring_v, const bna_tensor4* src_k,
+                     const bna_tensor4* src_v, int32_t dtype, int64_t pos0, int64_t ring, void* stream);
+
+/* Fused decode step for one new token per sequence: append k_new/v_new [B,Hkv,1,dh] at
+ * position `pos` into the ring, close block `close_block` into summary slot `close_slot`
+ * when close_block >= 0 (mean of its block_size tokens read from the ring), then attend
+ * q [B,Hq,1,dh] at position `pos` over the ring window and routed summaries (limit
+ * num_summary_limit, counting the block closed here). */
+BNA_API int bna_decode_step(const bna_tensor4* q, const bna_tensor4* k_new, const bna_tensor4* v_new,
+                    bna_tensor4* ring_k, bna_tensor4* ring_v, bna_tensor4* sum_k, bna_tensor4* sum_v,
+                    bna_tensor4* out, float* lse, int64_t lse_stride_b, int64_t lse_stride_h,
+                    int32_t dtype, const bna_route* route, int32_t window, int64_t pos, int64_t ring,
+                    int64_t close_block, int64_t close_slot, int32_t num_summary_limit, float scale,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BNA_B200_H */

@@ -26,3 +26,12 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(scope="session", autouse=True)
+def _built_library():
+    """Make sure libbna_b200.so exists (it is a build artefact, not committed)."""
+    from butterfly_b200 import build as _build
+    if not os.path.exists(os.path.join(ROOT, "butterfly_b200", "libbna_b200.so")):
+        _build.build()
+    yield
