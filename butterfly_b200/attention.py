@@ -119,14 +119,25 @@ def butterfly_compressed_attention(
     vs = block_mean_summaries(v, seq_len=T, block_size=BS, num_blocks=N)
     out = torch.empty((batch, T, H_q, dh), device=q.device, dtype=q.dtype).transpose(1, 2)
     lse = torch.empty((batch, H_q, T), device=q.device, dtype=torch.float32) if return_lse else None
-    lp, lb, lh = _lse_args(lse)
     sc = float(scale) if scale is not None else 1.0 / math.sqrt(dh)
-    tq, tk, tv, tks, tvs, to = (_lib.t4(x) for x in (q, k, v, ks, vs, out))
+    prefill_attention_into(q, k, v, ks, vs, out, lse, route, int(local_window_tokens), sc)
+    return (out, lse) if return_lse else out
+
+
+def prefill_attention_into(q, k, v, k_sum, v_sum, out, lse, route, window: int, scale: float, *,
+                           q_pos0: int = 0, kv_pos0: int = 0, total_len: Optional[int] = None) -> None:
+    """Launch the tcgen05 prefill kernel on pre-computed summaries (no allocation).
+
+    Query row i is at global position q_pos0 + i and key row j at kv_pos0 + j; the
+    routing covers a sequence of ``total_len`` tokens (default: q_pos0 + Tq)."""
+    T = int(q.shape[2])
+    tot = q_pos0 + T if total_len is None else int(total_len)
+    lp, lb, lh = _lse_args(lse)
+    tq, tk, tv, tks, tvs, to = (_lib.t4(x) for x in (q, k, v, k_sum, v_sum, out))
     _lib.check(_lib.lib().bna_prefill_attention(
         ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv), ctypes.byref(tks), ctypes.byref(tvs),
-        ctypes.byref(to), lp, lb, lh, dt, ctypes.byref(route), int(local_window_tokens), 0, 0, int(T),
-        sc, _lib.stream_ptr(q.device)))
-    return (out, lse) if return_lse else out
+        ctypes.byref(to), lp, lb, lh, _lib.dtype_code(q.dtype), ctypes.byref(route), int(window), int(q_pos0),
+        int(kv_pos0), tot, float(scale), _lib.stream_ptr(q.device)))
 
 
 def butterfly_compressed_attention_active(

@@ -1,0 +1,60 @@
+"""PyTorch-CPU restatement of the reference's vectorised compressed prefill — TEST
+INFRASTRUCTURE ONLY (the timed CPU baseline of ``bench.py --impl reference``).
+
+It follows the reference's own CPU algorithm (bna/torch/attention_wayfinder_permute.py
+:1046-1122): per-block index tensors (:912-966), fp32 block means cast to the input
+dtype (:1022-1043), a gather of each block's raw window and routed summaries, and one
+``F.scaled_dot_product_attention`` call with a boolean mask and GQA over the
+concatenated keys.  Its outputs are checked against the numpy oracle in the tests.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from .compressed import prefill_index_tensors
+
+
+def block_means_torch(x: torch.Tensor, block_size: int, num_blocks: int) -> torch.Tensor:
+    B, H, T, dh = x.shape
+    pad = num_blocks * block_size - T
+    xf = x.float()
+    if pad:
+        xf = F.pad(xf, (0, 0, 0, pad))
+    s = xf.view(B, H, num_blocks, block_size, dh).sum(dim=3)
+    cnt = torch.clamp(torch.minimum(torch.full((num_blocks,), block_size),
+                                    T - torch.arange(num_blocks) * block_size), min=1).float()
+    return (s / cnt.view(1, 1, -1, 1)).to(x.dtype)
+
+
+def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, neighbors, *, block_size: int,
+            window: int, block_chunk: int = 0, index_tensors=None) -> torch.Tensor:
+    B, Hq, T, dh = q.shape
+    Hkv = k.shape[1]
+    N = len(neighbors)
+    BS = block_size
+    if index_tensors is None:
+        index_tensors = [torch.from_numpy(np.ascontiguousarray(a))
+                         for a in prefill_index_tensors(neighbors, T, BS, window)]
+    raw_idx, raw_mask, sum_idx, sum_mask = index_tensors
+    R, S = raw_idx.shape[1], sum_idx.shape[1]
+    ks, vs = block_means_torch(k, BS, N), block_means_torch(v, BS, N)
+    pad = N * BS - T
+    qb = (F.pad(q, (0, 0, 0, pad)) if pad else q).view(B, Hq, N, BS, dh)
+    C = N if block_chunk <= 0 else min(block_chunk, N)
+    pieces = []
+    for c0 in range(0, N, C):
+        c1 = min(N, c0 + C)
+        n = c1 - c0
+        qc = qb[:, :, c0:c1].transpose(1, 2).reshape(B * n, Hq, BS, dh)
+        keys = torch.cat([k[:, :, raw_idx[c0:c1]], ks[:, :, sum_idx[c0:c1]]], dim=3)  # [B,Hkv,n,R+S,dh]
+        vals = torch.cat([v[:, :, raw_idx[c0:c1]], vs[:, :, sum_idx[c0:c1]]], dim=3)
+        keys = keys.transpose(1, 2).reshape(B * n, Hkv, R + S, dh)
+        vals = vals.transpose(1, 2).reshape(B * n, Hkv, R + S, dh)
+        mask = torch.cat([raw_mask[c0:c1], sum_mask[c0:c1]], dim=2)                       # [n,BS,R+S]
+        mask = mask.unsqueeze(0).expand(B, n, BS, R + S).reshape(B * n, 1, BS, R + S)
+        y = F.scaled_dot_product_attention(qc, keys, vals, attn_mask=mask, enable_gqa=Hkv < Hq)
+        pieces.append(y.view(B, n, Hq, BS, dh))
+    out = torch.cat(pieces, dim=1).transpose(1, 2).reshape(B, Hq, N * BS, dh)
+    return out[:, :, :T]

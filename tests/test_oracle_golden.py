@@ -111,3 +111,15 @@ def test_config1_full_size():
     np.testing.assert_allclose(out[:, :, G["c1_sample_pos"]], G["c1_sample_rows"], atol=3e-4, rtol=3e-4)
     np.testing.assert_allclose(out.astype(np.float64).sum(axis=(0, 2, 3)), G["c1_sum_per_head"], rtol=1e-4, atol=1e-2)
     np.testing.assert_allclose(np.abs(out.astype(np.float64)).sum(axis=(0, 2, 3)), G["c1_abssum_per_head"], rtol=1e-5)
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_torch_port_matches_reference(name):
+    import torch
+    from oracle import torch_port
+    c = _cfg(name)
+    pos = G[f"{name}_act_pos"]
+    q, k, v, _ = case_inputs(name, c["B"], c["Hq"], c["Hkv"], c["T"], c["dh"], pos)
+    y = torch_port.prefill(torch.from_numpy(q), torch.from_numpy(k), torch.from_numpy(v),
+                           G[f"{name}_neighbors"].tolist(), block_size=c["BS"], window=c["W"])
+    np.testing.assert_allclose(y.numpy(), G[f"{name}_out"], atol=3e-4, rtol=3e-4)
