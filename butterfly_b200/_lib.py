@@ -21,7 +21,7 @@ EXPORTED = (
     "bna_last_error", "bna_version", "bna_take_device_error", "bna_route_init",
     "bna_block_neighbors_host", "bna_prefill_selection_host", "bna_active_selection_host",
     "bna_prefill_selection_device", "bna_compress_blocks", "bna_prefill_attention",
-    "bna_active_attention", "bna_cache_append", "bna_decode_step",
+    "bna_active_attention", "bna_cache_append", "bna_decode_step", "bna_prefill_attention_static_scratch",
 )
 
 
@@ -68,6 +68,7 @@ def lib() -> ctypes.CDLL:
             "bna_prefill_attention": (i32, [T4, T4, T4, T4, T4, T4, vp, i64, i64, i32, R, i32, i64, i64, i64, f32, vp]),
             "bna_active_attention": (i32, [T4, T4, T4, T4, T4, T4, vp, i64, i64, i32, R, i32, vp, i64, i64, i64, i32, f32, vp]),
             "bna_cache_append": (i32, [T4, T4, T4, T4, i32, i64, i64, vp]),
+            "bna_prefill_attention_static_scratch": (i32, [T4, T4, T4, T4, vp, i64, i64, i32, R, i32, f32, vp]),
             "bna_decode_step": (i32, [T4, T4, T4, T4, T4, T4, T4, T4, vp, i64, i64, i32, R, i32, i64, i64, i64, i64, i32, f32, vp]),
         }
         for name, (res, args) in sig.items():
