@@ -344,10 +344,51 @@ def _traffic_from_profiles():
     return None
 
 
+def prefill_trace(dev):
+    """Per-unit pipeline timeline of one config-2 prefill launch (globaltimer stamps)."""
+    import ctypes
+    from butterfly_b200 import _lib
+    from butterfly_b200.attention import block_mean_summaries, prefill_attention_into, route_for
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(1, HQ, T, DH, device=dev, generator=g).bfloat16()
+    k = torch.randn(1, HKV, T, DH, device=dev, generator=g).bfloat16()
+    v = torch.randn(1, HKV, T, DH, device=dev, generator=g).bfloat16()
+    lay = _layouts(T)[5]
+    r = route_for(lay, dev)[0]
+    N = lay.num_blocks
+    ks = block_mean_summaries(k, seq_len=T, block_size=BS, num_blocks=N)
+    vs = block_mean_summaries(v, seq_len=T, block_size=BS, num_blocks=N)
+    out = torch.empty(1, T, HQ, DH, device=dev, dtype=torch.bfloat16).transpose(1, 2)
+    nsm = torch.cuda.get_device_properties(dev).multi_processor_count
+    buf = torch.zeros(nsm * 64 * 16, dtype=torch.int64, device=dev)
+    for _ in range(3):
+        prefill_attention_into(q, k, v, ks, vs, out, None, r, W, 1 / math.sqrt(DH))
+    _lib.lib().bna_set_prefill_trace(ctypes.c_void_p(buf.data_ptr()))
+    prefill_attention_into(q, k, v, ks, vs, out, None, r, W, 1 / math.sqrt(DH))
+    torch.cuda.synchronize()
+    _lib.lib().bna_set_prefill_trace(None)
+    tr = buf.view(nsm, 64, 16).cpu().numpy().astype("int64")
+    t0 = tr[:, :, :16][tr[:, :, :16] > 0].min()
+    names = ["prod_start", "v_landed", "prod_full", "mma_qk", "mma_pv", "smx_s", "smx_p", "smx_o", "smx_done",
+             "smx_ld", "smx_max", "smx_st_issued", "qk_landed", "smx_meta", "v_start", "v_full"]
+    for cta in (0,):
+        print(f"cta {cta} (us from kernel start)")
+        for i in range(16):
+            row = tr[cta, i, :16]
+            if row.max() == 0:
+                break
+            print(f"  unit {i:2d}: " + " ".join(f"{n}={(x - t0) / 1000:7.2f}" for n, x in zip(names, row) if n != "-" and x > 0))
+    end = tr[:, :, 8].max()
+    print(f"kernel span from first stamp: {(end - t0) / 1000:.2f} us")
+
+
 def profile_case(kind: str):
     """Small, self-terminating case for ncu captures (a few hundred MB on the device)."""
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if kind == "prefill-trace":
+        prefill_trace(dev)
+        return
     if kind == "prefill":
         import butterfly_b200 as bb
         from butterfly_b200.attention import block_mean_summaries, prefill_attention_into, route_for
@@ -382,7 +423,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--profile-case", choices=["prefill", "decode"], default=None,
+    ap.add_argument("--profile-case", choices=["prefill", "decode", "prefill-trace"], default=None,
                     help="small case for ncu: warm-up, then exactly one launch of the kernel")
     args = ap.parse_args()
     if args.profile_case:

@@ -18,7 +18,7 @@ BF16, F16 = 0, 1
 RULES = {"causal_shift": 0, "xor": 1, "bit_reversal": 2, "benes": 3}
 
 EXPORTED = (
-    "bna_last_error", "bna_version", "bna_take_device_error", "bna_route_init",
+    "bna_last_error", "bna_version", "bna_take_device_error", "bna_set_prefill_trace", "bna_route_init",
     "bna_block_neighbors_host", "bna_prefill_selection_host", "bna_active_selection_host",
     "bna_prefill_selection_device", "bna_compress_blocks", "bna_prefill_attention",
     "bna_active_attention", "bna_cache_append", "bna_decode_step", "bna_prefill_attention_static_scratch",
@@ -59,6 +59,7 @@ def lib() -> ctypes.CDLL:
             "bna_last_error": (ctypes.c_char_p, []),
             "bna_version": (ctypes.c_char_p, []),
             "bna_take_device_error": (i32, [i32, P32]),
+            "bna_set_prefill_trace": (i32, [vp]),
             "bna_route_init": (i32, [R, i32, i32, i32, i32, i32, i32, i32]),
             "bna_block_neighbors_host": (i32, [R, P32]),
             "bna_prefill_selection_host": (i32, [R, i32, i32, P32, P32, P32]),

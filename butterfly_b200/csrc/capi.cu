@@ -36,6 +36,7 @@ int launch_active(const bna_tensor4*, const bna_tensor4*, const bna_tensor4*, co
                   const bna_tensor4*, int64_t, int64_t, cudaStream_t);
 int launch_selection_dump(const bna_route*, int, int32_t*, int32_t*, cudaStream_t);
 int take_device_error(int, int32_t*);
+void set_prefill_trace(uint64_t*);
 
 // ---------------------------------------------------------------- validation helpers
 static bool null4(const bna_tensor4* t) { return t == nullptr || t->data == nullptr; }
@@ -90,6 +91,11 @@ const char* bna_version(void) { return "bna_b200 0.1.0 (sm_100a)"; }
 int bna_take_device_error(int device, int32_t* code_out) {
   if (!code_out) return fail(BNA_BAD_SHAPE, "code_out is null");
   return take_device_error(device, code_out);
+}
+
+int bna_set_prefill_trace(void* device_buffer) {
+  set_prefill_trace(static_cast<uint64_t*>(device_buffer));
+  return BNA_OK;
 }
 
 int bna_route_init(bna_route* r, int32_t seq_len, int32_t block_size, int32_t layer_idx, int32_t lwb,

@@ -9,9 +9,27 @@
 
 namespace bna {
 
+// 2^x in one MUFU instruction (flush-to-zero, ~2 ulp); exp2(-inf) = 0.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Two fp32 -> packed bf16x2 with round-to-nearest-even, on the integer ALU pipe (keeps the
+// conversion work off the transcendental pipe that the softmax exponentials saturate).
+// Inputs are finite.
+__device__ __forceinline__ uint32_t pack_bf16x2_alu(float a, float b) {
+  uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+  ua += 0x7FFFu + ((ua >> 16) & 1u);
+  ub += 0x7FFFu + ((ub >> 16) & 1u);
+  return __byte_perm(ua, ub, 0x7632);
+}
+
 template <typename T> struct ElemTraits;
 template <> struct ElemTraits<__nv_bfloat16> {
   static constexpr uint32_t kUmmaFormat = 1;
+  __device__ static __forceinline__ uint32_t pack2_fast(float a, float b) { return pack2(a, b); }
   __device__ static __forceinline__ uint32_t pack2(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -23,6 +41,7 @@ template <> struct ElemTraits<__nv_bfloat16> {
 };
 template <> struct ElemTraits<__half> {
   static constexpr uint32_t kUmmaFormat = 0;
+  __device__ static __forceinline__ uint32_t pack2_fast(float a, float b) { return pack2(a, b); }
   __device__ static __forceinline__ uint32_t pack2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);

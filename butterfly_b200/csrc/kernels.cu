@@ -48,7 +48,7 @@ __device__ __forceinline__ void block_mean(const View4& src, int b, int h, int64
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.f;
   if (tl < lanes) {
-#pragma unroll 4
+#pragma unroll 8
     for (int j = tl; j < count; j += lanes) {
       const int64_t pos = first_pos + j;
       const int64_t idx = ring > 0 ? pos % ring : pos - pos_base;
@@ -84,9 +84,13 @@ struct CompressArgs {
   int64_t pos0, valid_len, ring, slot0;
 };
 
+// 256 threads: 16 head_dim chunks x 16 token lanes, so a 128-token block is one round of
+// eight independent 128-bit loads per thread (all in flight together).
+constexpr int kCompressThreads = 256;
+
 template <typename T>
-__global__ void __launch_bounds__(128) compress_kernel(const CompressArgs a) {
-  __shared__ float red[128 * 8];
+__global__ void __launch_bounds__(kCompressThreads) compress_kernel(const CompressArgs a) {
+  __shared__ float red[kCompressThreads * 8];
   const int j = blockIdx.x;
   const int b = blockIdx.y / a.H, h = blockIdx.y % a.H;
   const int64_t first = a.pos0 + (int64_t)j * a.block_size;
@@ -286,9 +290,9 @@ int launch_compress(const bna_tensor4* x, bna_tensor4* out, int dtype, int block
   dim3 grid(n_blocks, (unsigned)(x->size[0] * x->size[1]));
   if (n_blocks == 0 || grid.y == 0) return BNA_OK;
   if (dtype == BNA_BF16)
-    compress_kernel<__nv_bfloat16><<<grid, 128, 0, stream>>>(a);
+    compress_kernel<__nv_bfloat16><<<grid, kCompressThreads, 0, stream>>>(a);
   else
-    compress_kernel<__half><<<grid, 128, 0, stream>>>(a);
+    compress_kernel<__half><<<grid, kCompressThreads, 0, stream>>>(a);
   return check_cuda(cudaGetLastError(), "compress_kernel launch");
 }
 

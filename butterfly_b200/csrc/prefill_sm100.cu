@@ -7,20 +7,25 @@
 // GQA: the G = Hq/Hkv query heads of a KV head share its keys.
 //
 // Work unit = (batch b, KV head, query tile of QT = 128/G positions).  Its 128 MMA rows
-// are the G heads x QT positions (M = 128).  The keys of the tile are one contiguous
-// slice of NR = round_up(W - 1 + QT, 16) raw positions starting at q0 - (W - 1), plus
-// a 16-row tile holding the block's routed summaries (zero rows where unused):
-//   S  = Q . [K_slice ; K_sum]^T   two tcgen05.mma chains into one TMEM tile (N = NR, 16)
-//   P  = masked softmax(S) (exp2, fp32 row sums), stored bf16/f16 to smem (SW128 K-major)
-//   O  = P . [V_slice ; V_sum]      tcgen05.mma with V as an MN-major operand
-// Loads: Q, K, V by TMA (128-byte swizzle, zero fill outside the tensor) into a
-// 2-stage ring; summaries by the producer warp with 128-bit loads.
+// are the G heads x QT positions (M = 128).  The keys of a unit are one contiguous slice
+// of NR = round_up(W - 1 + QT, 16) raw positions starting at q0 - (W - 1), followed by 16
+// rows holding the block's routed summaries (zero rows where unused), so
+//   S = Q . [K_slice ; K_sum]^T            one tcgen05.mma chain, N = NR + 16, fp32 in TMEM
+//   P = masked softmax(S)                  exp2 domain, fp32 row sums; P stored as 16-bit
+//                                          values back into the S columns of TMEM
+//   O = P . [V_slice ; V_sum]              tcgen05.mma with A = P read from TMEM and V an
+//                                          MN-major shared-memory operand
+// Loads: Q, K, V slices by TMA (128-byte swizzle, zero fill outside the tensor) into a
+// 2-stage ring; the summary rows by the producer warp with 128-bit loads written into the
+// same swizzled tiles.
 //
-// Warp roles (192 threads, one CTA per SM, persistent over units):
-//   warp 0      producer: TMA issue + summary rows
-//   warp 1      TMEM allocator + single-thread MMA issuer
-//   warps 2..5  softmax + epilogue (thread = TMEM lane = MMA row)
-// TMEM: S double buffer at columns [0,128) and [128,256), O at [256,384).
+// Warp roles (320 threads, one CTA per SM, persistent over units):
+//   warp 0       producer: TMA issue + summary rows
+//   warp 1       TMEM allocator + single-thread MMA issuer
+//   warps 2..5   softmax/epilogue group 0 (even local units)
+//   warps 6..9   softmax/epilogue group 1 (odd local units)
+// The two groups ping-pong so one group's softmax overlaps the other's MMAs and loads.
+// TMEM (512 columns): group g's S/P tile at [128g, 128g+128), its O tile at 256 + 128g.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -36,6 +41,7 @@ struct PrefillArgs {
   int QT, NR, ntiles, total_units, stages;
   int q_tmajor;  // Q tile rows ordered (position, head) instead of (head, position)
   int64_t q_pos0, kv_pos0, total_len;
+  int q_pos0_i, kidx0, blk0, tiles_per_block;  // 32-bit forms of the position math
   int window;
   float scale_log2;
   bna_route route;
@@ -46,22 +52,21 @@ struct PrefillArgs {
   int64_t os_b, os_h, os_t;
   float* lse;
   int64_t ls_b, ls_h;
-  int* err;  // device error word
+  int* err;         // device error word
+  uint64_t* trace;  // optional timeline: [cta][unit < 64][16] globaltimer stamps
 };
 
 struct PrefillSmem {
-  uint32_t q, kv_half, k, v, ks, vs, stage, p, p_bytes, bars, total;
+  uint32_t q, kv_rows, kv_half, k, v, stage, xchg, bars, total;
   __host__ __device__ PrefillSmem(int NR, int stages) {
-    q = 0;                        // 2 halves x 128 rows x 128 B
-    kv_half = (uint32_t)NR * 128;  // one 64-column half of a K or V slice
+    q = 0;                              // 2 halves x 128 rows x 128 B
+    kv_rows = (uint32_t)NR + 16;        // raw slice + summary rows
+    kv_half = kv_rows * 128;            // one 64-column half of a K or V tile
     k = 32768;
     v = k + 2 * kv_half;
-    ks = v + 2 * kv_half;          // 2 halves x 16 rows x 128 B
-    vs = ks + 4096;
-    stage = vs + 4096;
-    p = stage * stages;
-    p_bytes = ((NR + 16 + 63) / 64) * 16384;
-    bars = p + p_bytes;
+    stage = v + 2 * kv_half;
+    xchg = stage * stages;      // 4 x 256 floats of row max / sum exchange
+    bars = xchg + 4096;
     total = bars + 256 + 1024;  // + alignment slack
   }
 };
@@ -69,11 +74,13 @@ struct PrefillSmem {
 namespace {
 
 constexpr float kLn2 = 0.6931471805599453f;
+constexpr int kThreads = 608;  // 19 warps
+constexpr int kVWarp = 18;    // producer of the V part of each stage
 
-template <typename T>
-__global__ void __launch_bounds__(192, 1)
+template <typename T, int NR_>
+__global__ void __launch_bounds__(kThreads, 1)
     prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                         const __grid_constant__ CUtensorMap tmV, const PrefillArgs a) {
+                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ PrefillArgs a) {
   using namespace sm100;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -81,25 +88,32 @@ __global__ void __launch_bounds__(192, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
-  uint64_t* full = bars;        // [2] TMA + summaries landed
-  uint64_t* empty = bars + 2;   // [2] stage consumed by PV
-  uint64_t* sfull = bars + 4;   // [2] S tile ready in TMEM
-  uint64_t* pfull = bars + 6;   // P written to smem (128 arrivals)
-  uint64_t* ofull = bars + 7;   // O ready in TMEM
-  uint64_t* drain = bars + 8;   // MMA drain at exit
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 10);
+  uint64_t* full = bars;        // [2] Q + K part of a stage landed (TMA bytes + summary rows)
+  uint64_t* empty = bars + 2;   // [2] Q + K part consumed (QK done)
+  uint64_t* sfull = bars + 4;   // [2] per group: S ready in TMEM
+  uint64_t* pfull = bars + 6;   // [2] per group: P stored in TMEM (256 arrivals)
+  uint64_t* ofull = bars + 8;   // [2] per group: O ready in TMEM
+  uint64_t* drain = bars + 10;  // MMA drain at exit
+  uint64_t* vfull = bars + 11;  // [2] V part of a stage landed
+  uint64_t* vempty = bars + 13; // [2] V part consumed (PV done)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 16);
+  uint32_t* unit_meta = reinterpret_cast<uint32_t*>(bars + 17);  // [8] (unit << 8) | summary count
+  float* xchg = reinterpret_cast<float*>(smem + L.xchg);         // [2 groups][2 halves][256]
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
       mbar_init(&full[s], 2);
       mbar_init(&empty[s], 1);
+      mbar_init(&vfull[s], 2);
+      mbar_init(&vempty[s], 1);
       mbar_init(&sfull[s], 1);
+      mbar_init(&pfull[s], 256);
+      mbar_init(&ofull[s], 1);
     }
-    mbar_init(pfull, 128);
-    mbar_init(ofull, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
+    for (int k = 0; k < 8; ++k) unit_meta[k] = 0xFFFFFFFFu;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -109,31 +123,51 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmQ);
     prefetch_tmap(&tmK);
-    prefetch_tmap(&tmV);
   }
+  if (warp == kVWarp && lane == 0) prefetch_tmap(&tmV);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  const int NR = a.NR, QT = a.QT, G = a.G, S = a.stages;
+  constexpr int NK_ = NR_ + 16;  // keys per unit (raw slice + summary rows)
+  const int NR = NR_, QT = a.QT, G = a.G, S = a.stages;
+  const int NK = NK_;
+  auto stamp = [&](int i, int ev) {
+    if (a.trace && i < 64) a.trace[((int64_t)blockIdx.x * 64 + i) * 16 + ev] = globaltimer();
+  };
   const int BS = a.route.block_size;
   auto stage_ptr = [&](int s) { return smem + (uint32_t)s * L.stage; };
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
+    // Per unit: compute the routed summaries and fetch their rows into registers first
+    // (independent of the stage), then wait for the stage, issue the TMA loads and write
+    // the summary rows (zero rows past the valid ones) into the swizzled K/V tiles.
     int i = 0;
     for (int u = blockIdx.x; u < a.total_units; u += gridDim.x, ++i) {
       const int s = i % S;
       const uint32_t ph = (uint32_t)(i / S) & 1u;
-      if (i >= S && !mbar_wait(&empty[s], ph ^ 1u, abort_flag, 1, a.err)) break;
       const int t = u % a.ntiles, rest = u / a.ntiles, kvh = rest % a.Hkv, b = rest / a.Hkv;
       const int qs = t * QT;
-      const int64_t qg = a.q_pos0 + qs;
-      const int kidx = (int)(qg - (a.window - 1) - a.kv_pos0);
+      const int kidx = a.kidx0 + qs;
+      int ids[kMaxSummaries];
+      const int ns = prefill_summaries(a.route, a.blk0 + t / a.tiles_per_block, a.window, a.route.neighbors, ids);
+      const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.ksum) + 2 * (b * a.ks_b + kvh * a.ks_h);
+      const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.vsum) + 2 * (b * a.vs_b + kvh * a.vs_h);
+      uint4 kr[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = lane + 32 * j, r = c >> 4, ch = c & 15;
+        kr[j] = make_uint4(0, 0, 0, 0);
+        if (r < ns) kr[j] = ld_nc_128(kbase + 2 * (ids[r] * a.ks_n) + ch * 16);
+      }
+      (void)vbase;
+      if (i >= S && !mbar_wait(&empty[s], ph ^ 1u, abort_flag, 1, a.err)) break;
+      if (lane == 0) stamp(i, 0);
       uint8_t* st = stage_ptr(s);
       if (lane == 0) {
-        mbar_arrive_expect_tx(&full[s], 32768u + 4u * L.kv_half);
+        mbar_arrive_expect_tx(&full[s], 32768u + 2u * (uint32_t)NR * 128u);
         if (a.q_tmajor) {
           tma_load_4d(st + L.q, &tmQ, &full[s], 0, kvh * G, qs, b);
           tma_load_4d(st + L.q + 16384, &tmQ, &full[s], 64, kvh * G, qs, b);
@@ -143,81 +177,150 @@ __global__ void __launch_bounds__(192, 1)
         }
         tma_load_4d(st + L.k, &tmK, &full[s], 0, kidx, kvh, b);
         tma_load_4d(st + L.k + L.kv_half, &tmK, &full[s], 64, kidx, kvh, b);
-        tma_load_4d(st + L.v, &tmV, &full[s], 0, kidx, kvh, b);
-        tma_load_4d(st + L.v + L.kv_half, &tmV, &full[s], 64, kidx, kvh, b);
       }
-      int ids[kMaxSummaries];
-      const int blk = (int)(qg / BS);
-      const int ns = prefill_summaries(a.route, blk, a.window, a.route.neighbors, ids);
-      const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.ksum) + 2 * (b * a.ks_b + kvh * a.ks_h);
-      const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.vsum) + 2 * (b * a.vs_b + kvh * a.vs_h);
-#pragma unroll 4
-      for (int c = lane; c < 256; c += 32) {
-        const int r = c >> 4, ch = c & 15, half = ch >> 3, cc = ch & 7;
-        uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-        if (r < ns) {
-          kv = ld_nc_128(kbase + 2 * (ids[r] * a.ks_n) + ch * 16);
-          vv = ld_nc_128(vbase + 2 * (ids[r] * a.vs_n) + ch * 16);
-        }
-        const uint32_t off = half * 2048 + r * 128 + ((cc ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(st + L.ks + off) = kv;
-        *reinterpret_cast<uint4*>(st + L.vs + off) = vv;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = lane + 32 * j, r = c >> 4, ch = c & 15, half = ch >> 3, cc = ch & 7;
+        const int row = NR + r;
+        const uint32_t off = half * L.kv_half + row * 128 + ((cc ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(st + L.k + off) = kr[j];
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&full[s]);
+      if (lane == 0) {
+        stamp(i, 2);
+        *reinterpret_cast<volatile uint32_t*>(unit_meta + (i & 7)) = ((uint32_t)i << 8) | (uint32_t)ns;
+        mbar_arrive(&full[s]);
+      }
+    }
+  } else if (warp == kVWarp) {
+    // ------------------------------------------------------------------ V producer
+    int i = 0;
+    for (int u = blockIdx.x; u < a.total_units; u += gridDim.x, ++i) {
+      const int s = i % S;
+      const uint32_t ph = (uint32_t)(i / S) & 1u;
+      const int t = u % a.ntiles, rest = u / a.ntiles, kvh = rest % a.Hkv, b = rest / a.Hkv;
+      const int kidx = a.kidx0 + t * QT;
+      int ids[kMaxSummaries];
+      const int ns = prefill_summaries(a.route, a.blk0 + t / a.tiles_per_block, a.window, a.route.neighbors, ids);
+      const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.vsum) + 2 * (b * a.vs_b + kvh * a.vs_h);
+      uint4 vr[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = lane + 32 * j, r = c >> 4, ch = c & 15;
+        vr[j] = make_uint4(0, 0, 0, 0);
+        if (r < ns) vr[j] = ld_nc_128(vbase + 2 * (ids[r] * a.vs_n) + ch * 16);
+      }
+      if (i >= S && !mbar_wait(&vempty[s], ph ^ 1u, abort_flag, 10, a.err)) break;
+      if (lane == 0) stamp(i, 14);
+      uint8_t* st = stage_ptr(s);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&vfull[s], 2u * (uint32_t)NR * 128u);
+        tma_load_4d(st + L.v, &tmV, &vfull[s], 0, kidx, kvh, b);
+        tma_load_4d(st + L.v + L.kv_half, &tmV, &vfull[s], 64, kidx, kvh, b);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = lane + 32 * j, r = c >> 4, ch = c & 15, half = ch >> 3, cc = ch & 7;
+        const int row = NR + r;
+        const uint32_t off = half * L.kv_half + row * 128 + ((cc ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(st + L.v + off) = vr[j];
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        stamp(i, 15);
+        mbar_arrive(&vfull[s]);
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t fmt = ElemTraits<T>::kUmmaFormat;
-      const uint32_t id_qk = idesc_f16(128, NR, fmt, false);
-      const uint32_t id_qs = idesc_f16(128, 16, fmt, false);
+      const uint32_t id_qk = idesc_f16(128, NK, fmt, false);
       const uint32_t id_pv = idesc_f16(128, 128, fmt, true);
-      const uint32_t sP = smem_u32(smem + L.p);
       int n = 0;
       for (int u = blockIdx.x; u < a.total_units; u += gridDim.x) ++n;
       bool ok = true;
       auto issue_qk = [&](int i) -> bool {
-        const int s = i % S;
+        const int s = i % S, g = i & 1;
+        // S/P tile of group g was last read by PV(i - 2): wait for it before overwriting.
+        if (i >= 2 && !mbar_wait(&ofull[g], (uint32_t)((i - 2) >> 1) & 1u, abort_flag, 7, a.err)) return false;
         if (!mbar_wait(&full[s], (uint32_t)(i / S) & 1u, abort_flag, 2, a.err)) return false;
+        stamp(i, 3);
         tc_fence_after();
         const uint32_t base = smem_u32(stage_ptr(s));
-        const uint32_t dS = tmem + (uint32_t)(i & 1) * 128u;
+        const uint32_t dS = tmem + (uint32_t)g * 128u;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t kin = (uint32_t)(kk & 3) * 32u;
           const uint64_t aq = desc_sw128(base + L.q + (kk >> 2) * 16384u + kin, 16, 1024);
           const uint64_t bk = desc_sw128(base + L.k + (kk >> 2) * L.kv_half + kin, 16, 1024);
-          const uint64_t bs = desc_sw128(base + L.ks + (kk >> 2) * 2048u + kin, 16, 1024);
           mma_f16_ss(dS, aq, bk, id_qk, kk > 0);
-          mma_f16_ss(dS + (uint32_t)NR, aq, bs, id_qs, kk > 0);
         }
-        mma_commit(&sfull[i & 1]);
-        return true;
-      };
-      auto issue_pv = [&](int j) -> bool {
-        const int s = j % S;
-        if (!mbar_wait(pfull, (uint32_t)j & 1u, abort_flag, 3, a.err)) return false;
-        tc_fence_after();
-        const uint32_t base = smem_u32(stage_ptr(s));
-        const int nks = (NR + 16) / 16;
-        for (int ks = 0; ks < nks; ++ks) {
-          const uint64_t ap = desc_sw128(sP + (ks >> 2) * 16384u + (uint32_t)(ks & 3) * 32u, 16, 1024);
-          const uint64_t bv = (ks * 16 < NR) ? desc_sw128(base + L.v + (uint32_t)ks * 2048u, L.kv_half, 1024)
-                                             : desc_sw128(base + L.vs, 2048, 1024);
-          mma_f16_ss(tmem + 256u, ap, bv, id_pv, ks > 0);
-        }
-        mma_commit(ofull);
+        mma_commit(&sfull[g]);
         mma_commit(&empty[s]);
         return true;
       };
-      for (int i = 0; i < n && ok; ++i) {
-        ok = issue_qk(i);
-        if (ok && i > 0) ok = issue_pv(i - 1);
+      auto issue_pv = [&](int i) -> bool {
+        const int s = i % S, g = i & 1;
+        if (!mbar_wait(&pfull[g], (uint32_t)(i >> 1) & 1u, abort_flag, 3, a.err)) return false;
+        if (!mbar_wait(&vfull[s], (uint32_t)(i / S) & 1u, abort_flag, 9, a.err)) return false;
+        stamp(i, 4);
+        tc_fence_after();
+        const uint32_t base = smem_u32(stage_ptr(s));
+        const uint32_t aP = tmem + (uint32_t)g * 128u;
+        const uint32_t dO = tmem + 256u + (uint32_t)g * 128u;
+        for (int ks = 0; ks < NK / 16; ++ks) {
+          const uint64_t bv = desc_sw128(base + L.v + (uint32_t)ks * 2048u, L.kv_half, 1024);
+          mma_f16_ts(dO, aP + (uint32_t)ks * 8u, bv, id_pv, ks > 0);
+        }
+        mma_commit(&ofull[g]);
+        mma_commit(&vempty[s]);
+        return true;
+      };
+      // Issue whichever is ready: PV(j) once group j&1 stored P(j); QK(j) once unit j's
+      // stage landed and PV(j-2) (same S/P tile) completed.  PV is preferred.  With one
+      // stage, QK(j) also needs PV(j-1) issued (the stage is shared).
+      int next_qk = 0, next_pv = 0, seen_full = 0, seen_v = 0;
+      int64_t last = clock64();
+      uint32_t spins = 0;
+      while (next_pv < n && ok) {
+        bool progressed = false;
+        if (next_pv < next_qk && mbar_test_wait(&pfull[next_pv & 1], (uint32_t)(next_pv >> 1) & 1u) &&
+            mbar_test_wait(&vfull[next_pv % S], (uint32_t)(next_pv / S) & 1u)) {
+          ok = issue_pv(next_pv++);
+          progressed = true;
+        }
+        if (!progressed && next_pv < n && seen_v < next_pv + 1 &&
+            mbar_test_wait(&vfull[next_pv % S], (uint32_t)(next_pv / S) & 1u)) {
+          stamp(next_pv, 1);
+          seen_v = next_pv + 1;
+        }
+        if (!progressed && next_qk < n && seen_full < next_qk + 1 &&
+            mbar_test_wait(&full[next_qk % S], (uint32_t)(next_qk / S) & 1u)) {
+          stamp(next_qk, 12);
+          seen_full = next_qk + 1;
+        }
+        if (progressed) {
+        } else if (next_qk < n && next_qk < next_pv + 2 &&
+                   (next_qk < 2 || mbar_test_wait(&ofull[next_qk & 1], (uint32_t)((next_qk - 2) >> 1) & 1u)) &&
+                   mbar_test_wait(&full[next_qk % S], (uint32_t)(next_qk / S) & 1u)) {
+          ok = issue_qk(next_qk++);
+          progressed = true;
+        }
+        if (progressed) {
+          spins = 0;
+          last = clock64();
+        } else if ((++spins & 255) == 0) {
+          if (*abort_flag) break;
+          if (clock64() - last > kWaitTimeoutCycles) {
+            *abort_flag = 1;
+            if (a.err) atomicCAS(a.err, 0, 0x1000 | 8);
+            break;
+          }
+        }
       }
-      if (ok && n > 0) issue_pv(n - 1);
-      // Drain: every MMA issued above has completed once this commit arrives.
       volatile int never_abort = 0;
       mma_commit(drain);
       mbar_wait(drain, 0, &never_abort, 6, a.err);
@@ -225,102 +328,136 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
-    const int quad = warp & 3;
+    // Group grp handles local units i with i % 2 == grp.  Its 8 warps pair up per TMEM lane
+    // quarter: half 0 takes S columns [0, kHalf0) and O columns [0, 64), half 1 the rest.
+    // The two threads of a row exchange partial max / sum through shared memory, synced
+    // by a 64-thread named barrier per (group, quarter).
+    constexpr int kHalf0 = ((NK_ / 16 + 1) / 2) * 16;
+    const int gw = warp - 2;
+    const int grp = gw >> 3;
+    const int half = (gw >> 2) & 1;
+    const int quad = warp & 3;  // TMEM lane quarter this warp may access
     const int row = quad * 32 + lane;
-    const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16);
-    uint8_t* sP = smem + L.p;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t tS = tmem + lane_off + (uint32_t)grp * 128u;
+    const uint32_t tO = tmem + lane_off + 256u + (uint32_t)grp * 128u;
     const int g = a.q_tmajor ? (row % G) : (row / QT);
     const int qi = a.q_tmajor ? (row / G) : (row % QT);
+    float* xm = xchg + (grp * 2 + half) * 256;        // my partial max [0,128) / sum [128,256)
+    float* xo = xchg + (grp * 2 + (half ^ 1)) * 256;  // partner's
+    const uint32_t bar_id = 1u + (uint32_t)(grp * 4 + quad);
+    const float sl2 = a.scale_log2;
     int i = 0;
     for (int u = blockIdx.x; u < a.total_units; u += gridDim.x, ++i) {
-      if (!mbar_wait(&sfull[i & 1], (uint32_t)(i >> 1) & 1u, abort_flag, 4, a.err)) break;
-      tc_fence_after();
+      if ((i & 1) != grp) continue;
+      const uint32_t par = (uint32_t)(i >> 1) & 1u;
       const int t = u % a.ntiles, rest = u / a.ntiles, kvh = rest % a.Hkv, b = rest / a.Hkv;
       const int qs = t * QT;
       const int qloc = qs + qi;
       const bool valid_row = qloc < a.Tq;
-      const int64_t qglob = a.q_pos0 + qloc;
-      const int64_t kstart = a.q_pos0 + qs - (a.window - 1);
-      int ids[kMaxSummaries];
-      const int ns = prefill_summaries(a.route, (int)((a.q_pos0 + qs) / BS), a.window, a.route.neighbors, ids);
-      const int lo = (int)(max64(0, qglob - a.window + 1) - kstart);
-      const int hi = (int)(qglob - kstart);
-      const uint32_t sAddr = lane_addr + (uint32_t)(i & 1) * 128u;
-
-      float m = -INFINITY;
-      for (int c0 = 0; c0 < NR; c0 += 16) {
-        float x[16];
-        tmem_ld16(sAddr + c0, x);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (c0 + j >= lo && c0 + j <= hi) m = fmaxf(m, x[j]);
-      }
+      // positions fit in 32 bits (checked on the host); no 64-bit division on this path
+      const int qglob = a.q_pos0_i + qloc;
+      const int kstart = a.q_pos0_i + qs - (a.window - 1);
+      const int lo = max(0, qglob - a.window + 1) - kstart;
+      const int hi = qglob - kstart;
+      if (row == 0 && half == 0) stamp(i, 13);
+      if (!mbar_wait(&sfull[grp], par, abort_flag, 4, a.err)) break;
+      // routed-summary count of this unit, published by the producer (tagged word)
+      int ns = 0;
       {
-        float x[16];
-        tmem_ld16(sAddr + NR, x);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (j < ns) m = fmaxf(m, x[j]);
+        const volatile uint32_t* slot = unit_meta + (i & 7);
+        uint32_t w = *slot;
+        for (int spin = 0; (w >> 8) != (uint32_t)i && spin < (1 << 22); ++spin) w = *slot;
+        ns = (int)(w & 0xFFu);
       }
-      const float mb = valid_row ? m * a.scale_log2 : 0.f;
-      float l = 0.f;
-      for (int c0 = 0; c0 < NR + 16; c0 += 16) {
-        float x[16];
-        tmem_ld16(sAddr + c0, x);
-        tmem_ld_wait();
-        uint32_t pk[8];
+      if (row == 0 && half == 0) stamp(i, 5);
+      tc_fence_after();
+      const uint32_t wlo = valid_row ? (uint32_t)lo : 1u;
+      const uint32_t wspan = valid_row ? (uint32_t)(hi - lo) : 0u;
+      const int nsv = valid_row ? ns : 0;
+
+      // S columns of my half in registers; masked entries become -inf.
+      constexpr int kMaxCols = kHalf0 > NK_ - kHalf0 ? kHalf0 : NK_ - kHalf0;
+      const int cbeg = half ? kHalf0 : 0;
+      float x[kMaxCols];
+      float mp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (half == 0) {
 #pragma unroll
-        for (int j = 0; j < 16; j += 2) {
-          float p0, p1;
-          const int c = c0 + j;
-          bool v0, v1;
-          if (c0 < NR) {
-            v0 = c >= lo && c <= hi;
-            v1 = c + 1 >= lo && c + 1 <= hi;
-          } else {
-            v0 = j < ns;
-            v1 = j + 1 < ns;
-          }
-          v0 = v0 && valid_row;
-          v1 = v1 && valid_row;
-          p0 = v0 ? exp2f(fmaf(x[j], a.scale_log2, -mb)) : 0.f;
-          p1 = v1 ? exp2f(fmaf(x[j + 1], a.scale_log2, -mb)) : 0.f;
-          l += p0 + p1;
-          pk[j >> 1] = ElemTraits<T>::pack2(p0, p1);
+        for (int c0 = 0; c0 < kHalf0; c0 += 16) tmem_ld16(tS + c0, x + c0);
+      } else {
+#pragma unroll
+        for (int c0 = kHalf0; c0 < NK_; c0 += 16) tmem_ld16(tS + c0, x + (c0 - kHalf0));
+      }
+      tmem_ld_wait();
+#pragma unroll
+      for (int k = 0; k < kMaxCols; ++k) {
+        const int c = cbeg + k;  // uniform per warp
+        if (c < NK_) {
+          const bool v = c < NR_ ? ((uint32_t)c - wlo <= wspan) : (c - NR_ < nsv);
+          x[k] = v ? x[k] : -INFINITY;
+          mp[k & 3] = fmaxf(mp[k & 3], x[k]);
         }
-        const int half = c0 >> 6, cc = (c0 & 63) >> 3;
-        uint8_t* base = sP + half * 16384 + row * 128;
-        *reinterpret_cast<uint4*>(base + ((cc ^ (row & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *reinterpret_cast<uint4*>(base + (((cc + 1) ^ (row & 7)) << 4)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
-      fence_proxy_async_smem();
+      float m = fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3]));
+      xm[row] = m;
+      named_bar_sync(bar_id, 64);
+      m = fmaxf(m, xo[row]);
+      const float mb = m > -INFINITY ? m * sl2 : 0.f;
+      if (row == 0 && half == 0) stamp(i, 10);
+      float lp[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int k0 = 0; k0 < kMaxCols; k0 += 16) {
+        const int c0 = cbeg + k0;
+        if (c0 < NK_ && (half == 1 || c0 < kHalf0)) {
+          uint32_t pk[8];
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            const float p0 = ex2_approx(fmaf(x[k0 + j], sl2, -mb));
+            const float p1 = ex2_approx(fmaf(x[k0 + j + 1], sl2, -mb));
+            lp[(j >> 1) & 3] += p0 + p1;
+            pk[j >> 1] = ElemTraits<T>::pack2_fast(p0, p1);
+          }
+          tmem_st8(tS + (uint32_t)(c0 >> 1), pk);
+        }
+      }
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(pfull);
-      if (!mbar_wait(ofull, (uint32_t)i & 1u, abort_flag, 5, a.err)) break;
+      mbar_arrive(&pfull[grp]);
+      if (row == 0 && half == 0) stamp(i, 6);
+      float l = (lp[0] + lp[1]) + (lp[2] + lp[3]);
+      xm[128 + row] = l;
+      named_bar_sync(bar_id, 64);
+      l += xo[128 + row];
+
+      if (!mbar_wait(&ofull[grp], par, abort_flag, 5, a.err)) break;
+      if (row == 0 && half == 0) stamp(i, 7);
       tc_fence_after();
       const float inv = (valid_row && l > 0.f) ? 1.f / l : 0.f;
       uint8_t* orow = reinterpret_cast<uint8_t*>(a.out) +
-                      2 * (b * a.os_b + (int64_t)(kvh * G + g) * a.os_h + (int64_t)qloc * a.os_t);
-      for (int c0 = 0; c0 < 128; c0 += 16) {
-        float x[16];
-        tmem_ld16(lane_addr + 256u + c0, x);
+                      2 * (b * a.os_b + (int64_t)(kvh * G + g) * a.os_h + (int64_t)qloc * a.os_t) + half * 128;
+      {
+        float o[64];
+#pragma unroll
+        for (int c0 = 0; c0 < 64; c0 += 16) tmem_ld16(tO + half * 64 + c0, o + c0);
         tmem_ld_wait();
         if (valid_row) {
-          uint32_t pk[8];
 #pragma unroll
-          for (int j = 0; j < 16; j += 2) pk[j >> 1] = ElemTraits<T>::pack2(x[j] * inv, x[j + 1] * inv);
-          st_128(orow + c0 * 2, make_uint4(pk[0], pk[1], pk[2], pk[3]));
-          st_128(orow + c0 * 2 + 16, make_uint4(pk[4], pk[5], pk[6], pk[7]));
+          for (int c0 = 0; c0 < 64; c0 += 8) {
+            uint4 w;
+            w.x = ElemTraits<T>::pack2_fast(o[c0] * inv, o[c0 + 1] * inv);
+            w.y = ElemTraits<T>::pack2_fast(o[c0 + 2] * inv, o[c0 + 3] * inv);
+            w.z = ElemTraits<T>::pack2_fast(o[c0 + 4] * inv, o[c0 + 5] * inv);
+            w.w = ElemTraits<T>::pack2_fast(o[c0 + 6] * inv, o[c0 + 7] * inv);
+            st_128(orow + c0 * 2, w);
+          }
         }
       }
-      if (valid_row && a.lse)
+      if (valid_row && a.lse && half == 0)
         a.lse[b * a.ls_b + (int64_t)(kvh * G + g) * a.ls_h + qloc] = (mb + log2f(l)) * kLn2;
+      if (row == 0 && half == 0) stamp(i, 8);
       tc_fence_before();
     }
   }
-
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -333,6 +470,11 @@ __global__ void __launch_bounds__(192, 1)
 
 // ----------------------------------------------------------------------------- host
 int* device_error_word();  // kernels.cu
+
+// Optional prefill timeline buffer (device, >= grid * 64 * 16 uint64), set by
+// bna_set_prefill_trace; nullptr disables the stamps.
+static uint64_t* g_prefill_trace = nullptr;
+void set_prefill_trace(uint64_t* p) { g_prefill_trace = p; }
 using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
 
 static EncodeFn get_encode() {
@@ -387,6 +529,8 @@ int launch_prefill(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4
   a.NR = ((window - 1 + a.QT) + 15) / 16 * 16;
   if (a.NR + 16 > 256)
     return fail(BNA_UNSUPPORTED, "window too large for one tensor-core key tile (need W - 1 + 128/G + 16 <= 256)");
+  if (total_len >= (int64_t)1 << 30 || kv_pos0 + k->size[2] >= (int64_t)1 << 30)
+    return fail(BNA_UNSUPPORTED, "sequences of 2^30 tokens or more");
   if (route->block_size % a.QT != 0 || q_pos0 % route->block_size != 0)
     return fail(BNA_UNSUPPORTED, "block_size must be a multiple of 128/G and q_pos0 a multiple of block_size");
   a.ntiles = (a.Tq + a.QT - 1) / a.QT;
@@ -396,6 +540,10 @@ int launch_prefill(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4
   a.kv_pos0 = kv_pos0;
   a.total_len = total_len;
   a.window = window;
+  a.q_pos0_i = (int)q_pos0;
+  a.kidx0 = (int)(q_pos0 - (window - 1) - kv_pos0);
+  a.blk0 = (int)(q_pos0 / route->block_size);
+  a.tiles_per_block = route->block_size / a.QT;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.route = *route;
   a.ksum = ks->data;
@@ -408,6 +556,8 @@ int launch_prefill(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4
   a.ls_b = ls_b;
   a.ls_h = ls_h;
   a.err = device_error_word();
+  a.trace = g_prefill_trace;
+
 
   int dev = 0, nsm = 0, max_smem = 0;
   cudaGetDevice(&dev);
@@ -439,15 +589,24 @@ int launch_prefill(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4
   if ((rc = encode_map(&mv, v, dt, okv, bkv, "v"))) return rc;
 
   const int grid = a.total_units < nsm ? a.total_units : nsm;
-  if (dtype == BNA_BF16) {
-    auto kern = prefill_sm100_kernel<__nv_bfloat16>;
+  auto launch = [&](auto kern) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<grid, 192, smem, stream>>>(mq, mk, mv, a);
-  } else {
-    auto kern = prefill_sm100_kernel<__half>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<grid, 192, smem, stream>>>(mq, mk, mv, a);
+    kern<<<grid, kThreads, smem, stream>>>(mq, mk, mv, a);
+  };
+#define BNA_PREFILL_CASE(NRV)                                          \
+  case NRV:                                                            \
+    if (dtype == BNA_BF16) launch(prefill_sm100_kernel<__nv_bfloat16, NRV>); \
+    else launch(prefill_sm100_kernel<__half, NRV>);                    \
+    break;
+  switch (a.NR) {
+    BNA_PREFILL_CASE(16) BNA_PREFILL_CASE(32) BNA_PREFILL_CASE(48) BNA_PREFILL_CASE(64)
+    BNA_PREFILL_CASE(80) BNA_PREFILL_CASE(96) BNA_PREFILL_CASE(112) BNA_PREFILL_CASE(128)
+    BNA_PREFILL_CASE(144) BNA_PREFILL_CASE(160) BNA_PREFILL_CASE(176) BNA_PREFILL_CASE(192)
+    BNA_PREFILL_CASE(208) BNA_PREFILL_CASE(224) BNA_PREFILL_CASE(240)
+    default:
+      return fail(BNA_UNSUPPORTED, "unsupported key-slice width");
   }
+#undef BNA_PREFILL_CASE
   return check_cuda(cudaGetLastError(), "prefill_sm100_kernel launch");
 }
 

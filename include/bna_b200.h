@@ -87,6 +87,11 @@ BNA_API const char* bna_version(void);
  * wait (0 = none).  Synchronises the given device. */
 BNA_API int bna_take_device_error(int device, int32_t* code_out);
 
+/* Tracing: when non-NULL, later prefill launches write globaltimer stamps of each work
+ * unit's pipeline hand-offs to this device buffer ([grid][64 units][16] uint64, grid =
+ * number of SMs).  Pass NULL to stop.  Used by the profiling tools only. */
+BNA_API int bna_set_prefill_trace(void* device_buffer);
+
 /* ---- topology / selection (host) -------------------------------------------------- */
 
 /* Fill `route` (everything but `neighbors`) for a layer; replaces
