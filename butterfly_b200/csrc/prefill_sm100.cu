@@ -139,11 +139,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int BS = a.route.block_size;
   auto stage_ptr = [&](int s) { return smem + (uint32_t)s * L.stage; };
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ producer
-    // Per unit: compute the routed summaries and fetch their rows into registers first
-    // (independent of the stage), then wait for the stage, issue the TMA loads and write
-    // the summary rows (zero rows past the valid ones) into the swizzled K/V tiles.
+  if (warp == 0 || warp == kVWarp) {
+    // ------------------------------------------------------------------ producers
+    // Warp 0 fills the Q + K part of each stage, warp kVWarp the V part.  Both append the
+    // unit's routed-summary rows (zero rows past the valid ones) to their K / V tile.
+    // Software-pipelined by one unit: the route and the summary-row loads of unit i+1 are
+    // issued before waiting for unit i's stage, so their latency is off the critical path.
+    const bool isv = warp == kVWarp;
+    const uint8_t* sumbase = reinterpret_cast<const uint8_t*>(isv ? a.vsum : a.ksum);
+    const int64_t sb_ = isv ? a.vs_b : a.ks_b, sh_ = isv ? a.vs_h : a.ks_h, sn_ = isv ? a.vs_n : a.ks_n;
+    uint64_t* fullb = isv ? vfull : full;
+    uint64_t* emptyb = isv ? vempty : empty;
+    const uint32_t tile_off = isv ? L.v : L.k;
+    uint4 cur[8], nxt[8];
+    int ns_cur = 0, ns_nxt = 0;
+    auto fetch = [&](int u, uint4* regs) -> int {
+      const int t = u % a.ntiles, rest = u / a.ntiles, kvh = rest % a.Hkv, b = rest / a.Hkv;
+      int ids[kMaxSummaries];
+      const int ns = prefill_summaries(a.route, a.blk0 + t / a.tiles_per_block, a.window, a.route.neighbors, ids);
+      const uint8_t* base = sumbase + 2 * (b * sb_ + kvh * sh_);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = lane + 32 * j, r = c >> 4, ch = c & 15;
+        regs[j] = make_uint4(0, 0, 0, 0);
+        if (r < ns) regs[j] = ld_nc_128(base + 2 * (ids[r] * sn_) + ch * 16);
+      }
+      return ns;
+    };
+    if ((int)blockIdx.x < a.total_units) ns_cur = fetch(blockIdx.x, cur);
     int i = 0;
     for (int u = blockIdx.x; u < a.total_units; u += gridDim.x, ++i) {
       const int s = i % S;
@@ -151,87 +174,45 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int t = u % a.ntiles, rest = u / a.ntiles, kvh = rest % a.Hkv, b = rest / a.Hkv;
       const int qs = t * QT;
       const int kidx = a.kidx0 + qs;
-      int ids[kMaxSummaries];
-      const int ns = prefill_summaries(a.route, a.blk0 + t / a.tiles_per_block, a.window, a.route.neighbors, ids);
-      const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.ksum) + 2 * (b * a.ks_b + kvh * a.ks_h);
-      const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.vsum) + 2 * (b * a.vs_b + kvh * a.vs_h);
-      uint4 kr[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int c = lane + 32 * j, r = c >> 4, ch = c & 15;
-        kr[j] = make_uint4(0, 0, 0, 0);
-        if (r < ns) kr[j] = ld_nc_128(kbase + 2 * (ids[r] * a.ks_n) + ch * 16);
-      }
-      (void)vbase;
-      if (i >= S && !mbar_wait(&empty[s], ph ^ 1u, abort_flag, 1, a.err)) break;
-      if (lane == 0) stamp(i, 0);
+      if (u + (int)gridDim.x < a.total_units) ns_nxt = fetch(u + gridDim.x, nxt);
+      if (i >= S && !mbar_wait(&emptyb[s], ph ^ 1u, abort_flag, isv ? 10 : 1, a.err)) break;
+      if (lane == 0) stamp(i, isv ? 14 : 0);
       uint8_t* st = stage_ptr(s);
       if (lane == 0) {
-        mbar_arrive_expect_tx(&full[s], 32768u + 2u * (uint32_t)NR * 128u);
-        if (a.q_tmajor) {
-          tma_load_4d(st + L.q, &tmQ, &full[s], 0, kvh * G, qs, b);
-          tma_load_4d(st + L.q + 16384, &tmQ, &full[s], 64, kvh * G, qs, b);
+        if (!isv) {
+          mbar_arrive_expect_tx(&full[s], 32768u + 2u * (uint32_t)NR * 128u);
+          if (a.q_tmajor) {
+            tma_load_4d(st + L.q, &tmQ, &full[s], 0, kvh * G, qs, b);
+            tma_load_4d(st + L.q + 16384, &tmQ, &full[s], 64, kvh * G, qs, b);
+          } else {
+            tma_load_4d(st + L.q, &tmQ, &full[s], 0, qs, kvh * G, b);
+            tma_load_4d(st + L.q + 16384, &tmQ, &full[s], 64, qs, kvh * G, b);
+          }
+          tma_load_4d(st + L.k, &tmK, &full[s], 0, kidx, kvh, b);
+          tma_load_4d(st + L.k + L.kv_half, &tmK, &full[s], 64, kidx, kvh, b);
         } else {
-          tma_load_4d(st + L.q, &tmQ, &full[s], 0, qs, kvh * G, b);
-          tma_load_4d(st + L.q + 16384, &tmQ, &full[s], 64, qs, kvh * G, b);
+          mbar_arrive_expect_tx(&vfull[s], 2u * (uint32_t)NR * 128u);
+          tma_load_4d(st + L.v, &tmV, &vfull[s], 0, kidx, kvh, b);
+          tma_load_4d(st + L.v + L.kv_half, &tmV, &vfull[s], 64, kidx, kvh, b);
         }
-        tma_load_4d(st + L.k, &tmK, &full[s], 0, kidx, kvh, b);
-        tma_load_4d(st + L.k + L.kv_half, &tmK, &full[s], 64, kidx, kvh, b);
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int c = lane + 32 * j, r = c >> 4, ch = c & 15, half = ch >> 3, cc = ch & 7;
         const int row = NR + r;
         const uint32_t off = half * L.kv_half + row * 128 + ((cc ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(st + L.k + off) = kr[j];
+        *reinterpret_cast<uint4*>(st + tile_off + off) = cur[j];
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        stamp(i, 2);
-        *reinterpret_cast<volatile uint32_t*>(unit_meta + (i & 7)) = ((uint32_t)i << 8) | (uint32_t)ns;
-        mbar_arrive(&full[s]);
-      }
-    }
-  } else if (warp == kVWarp) {
-    // ------------------------------------------------------------------ V producer
-    int i = 0;
-    for (int u = blockIdx.x; u < a.total_units; u += gridDim.x, ++i) {
-      const int s = i % S;
-      const uint32_t ph = (uint32_t)(i / S) & 1u;
-      const int t = u % a.ntiles, rest = u / a.ntiles, kvh = rest % a.Hkv, b = rest / a.Hkv;
-      const int kidx = a.kidx0 + t * QT;
-      int ids[kMaxSummaries];
-      const int ns = prefill_summaries(a.route, a.blk0 + t / a.tiles_per_block, a.window, a.route.neighbors, ids);
-      const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.vsum) + 2 * (b * a.vs_b + kvh * a.vs_h);
-      uint4 vr[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int c = lane + 32 * j, r = c >> 4, ch = c & 15;
-        vr[j] = make_uint4(0, 0, 0, 0);
-        if (r < ns) vr[j] = ld_nc_128(vbase + 2 * (ids[r] * a.vs_n) + ch * 16);
-      }
-      if (i >= S && !mbar_wait(&vempty[s], ph ^ 1u, abort_flag, 10, a.err)) break;
-      if (lane == 0) stamp(i, 14);
-      uint8_t* st = stage_ptr(s);
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&vfull[s], 2u * (uint32_t)NR * 128u);
-        tma_load_4d(st + L.v, &tmV, &vfull[s], 0, kidx, kvh, b);
-        tma_load_4d(st + L.v + L.kv_half, &tmV, &vfull[s], 64, kidx, kvh, b);
+        stamp(i, isv ? 15 : 2);
+        if (!isv) *reinterpret_cast<volatile uint32_t*>(unit_meta + (i & 7)) = ((uint32_t)i << 8) | (uint32_t)ns_cur;
+        mbar_arrive(&fullb[s]);
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int c = lane + 32 * j, r = c >> 4, ch = c & 15, half = ch >> 3, cc = ch & 7;
-        const int row = NR + r;
-        const uint32_t off = half * L.kv_half + row * 128 + ((cc ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(st + L.v + off) = vr[j];
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        stamp(i, 15);
-        mbar_arrive(&vfull[s]);
-      }
+      for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+      ns_cur = ns_nxt;
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
