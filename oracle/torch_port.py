@@ -24,7 +24,7 @@ def block_means_torch(x: torch.Tensor, block_size: int, num_blocks: int) -> torc
         xf = F.pad(xf, (0, 0, 0, pad))
     s = xf.view(B, H, num_blocks, block_size, dh).sum(dim=3)
     cnt = torch.clamp(torch.minimum(torch.full((num_blocks,), block_size),
-                                    T - torch.arange(num_blocks) * block_size), min=1).float()
+                                    T - torch.arange(num_blocks) * block_size), min=1).float().to(x.device)
     return (s / cnt.view(1, 1, -1, 1)).to(x.dtype)
 
 
@@ -35,7 +35,7 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, neighbors, *, blo
     N = len(neighbors)
     BS = block_size
     if index_tensors is None:
-        index_tensors = [torch.from_numpy(np.ascontiguousarray(a))
+        index_tensors = [torch.from_numpy(np.ascontiguousarray(a)).to(q.device)
                          for a in prefill_index_tensors(neighbors, T, BS, window)]
     raw_idx, raw_mask, sum_idx, sum_mask = index_tensors
     R, S = raw_idx.shape[1], sum_idx.shape[1]
@@ -58,3 +58,22 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, neighbors, *, blo
         pieces.append(y.view(B, n, Hq, BS, dh))
     out = torch.cat(pieces, dim=1).transpose(1, 2).reshape(B, Hq, N * BS, dh)
     return out[:, :, :T]
+
+
+def active(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, neighbors, positions, *, block_size: int,
+           window: int) -> torch.Tensor:
+    """Active rows over a full K/V history, restating :1125-1197 (gather + masked SDPA)."""
+    from .compressed import active_index_tensors
+    B, Hq, Tq, dh = q.shape
+    Hkv, Tk = k.shape[1], k.shape[2]
+    N = len(neighbors)
+    ri, rm, si, sm = [torch.from_numpy(np.ascontiguousarray(a)).to(q.device) for a in
+                      active_index_tensors(neighbors, Tk, [int(p) for p in positions], block_size, window)]
+    ks, vs = block_means_torch(k, block_size, N), block_means_torch(v, block_size, N)
+    R, S = ri.shape[1], si.shape[1]
+    keys = torch.cat([k[:, :, ri], ks[:, :, si]], dim=3).transpose(1, 2).reshape(B * Tq, Hkv, R + S, dh)
+    vals = torch.cat([v[:, :, ri], vs[:, :, si]], dim=3).transpose(1, 2).reshape(B * Tq, Hkv, R + S, dh)
+    qr = q.transpose(1, 2).reshape(B * Tq, Hq, 1, dh)
+    mask = torch.cat([rm, sm], dim=1).unsqueeze(0).expand(B, Tq, R + S).reshape(B * Tq, 1, 1, R + S)
+    y = F.scaled_dot_product_attention(qr, keys, vals, attn_mask=mask, enable_gqa=Hkv < Hq)
+    return y.reshape(B, Tq, Hq, dh).transpose(1, 2)
