@@ -77,3 +77,26 @@ def active(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, neighbors, positio
     mask = torch.cat([rm, sm], dim=1).unsqueeze(0).expand(B, Tq, R + S).reshape(B * Tq, 1, 1, R + S)
     y = F.scaled_dot_product_attention(qr, keys, vals, attn_mask=mask, enable_gqa=Hkv < Hq)
     return y.reshape(B, Tq, Hq, dh).transpose(1, 2)
+
+
+def prefill_shard(q: torch.Tensor, k_ext: torch.Tensor, v_ext: torch.Tensor, k_sum: torch.Tensor,
+                  v_sum: torch.Tensor, neighbors, *, block_size: int, window: int, q_pos0: int, kv_pos0: int,
+                  total_len: int) -> torch.Tensor:
+    """The reference prefill restricted to queries [q_pos0, q_pos0 + Tq) of a total_len-token
+    sequence, with keys given from global position kv_pos0 and global block means supplied."""
+    B, Hq, Tq, dh = q.shape
+    Hkv = k_ext.shape[1]
+    BS = block_size
+    raw_idx, raw_mask, sum_idx, sum_mask = [torch.from_numpy(np.ascontiguousarray(a)).to(q.device)
+                                            for a in prefill_index_tensors(neighbors, total_len, BS, window)]
+    b0, nb = q_pos0 // BS, -(-Tq // BS)
+    raw_idx = (raw_idx[b0:b0 + nb] - kv_pos0).clamp(0, k_ext.shape[2] - 1)
+    raw_mask, sum_idx, sum_mask = raw_mask[b0:b0 + nb], sum_idx[b0:b0 + nb], sum_mask[b0:b0 + nb]
+    R, S = raw_idx.shape[1], sum_idx.shape[1]
+    pad = nb * BS - Tq
+    qb = (F.pad(q, (0, 0, 0, pad)) if pad else q).view(B, Hq, nb, BS, dh).transpose(1, 2).reshape(B * nb, Hq, BS, dh)
+    keys = torch.cat([k_ext[:, :, raw_idx], k_sum[:, :, sum_idx]], dim=3).transpose(1, 2).reshape(B * nb, Hkv, R + S, dh)
+    vals = torch.cat([v_ext[:, :, raw_idx], v_sum[:, :, sum_idx]], dim=3).transpose(1, 2).reshape(B * nb, Hkv, R + S, dh)
+    mask = torch.cat([raw_mask, sum_mask], dim=2).unsqueeze(0).expand(B, nb, BS, R + S).reshape(B * nb, 1, BS, R + S)
+    y = F.scaled_dot_product_attention(qb, keys, vals, attn_mask=mask, enable_gqa=Hkv < Hq)
+    return y.view(B, nb, Hq, BS, dh).transpose(1, 2).reshape(B, Hq, nb * BS, dh)[:, :, :Tq]

@@ -223,3 +223,23 @@ def test_no_device_error_word_left():
     code = ctypes.c_int32(-1)
     _lib.check(_lib.lib().bna_take_device_error(torch.cuda.current_device(), ctypes.byref(code)))
     assert code.value == 0
+
+
+def test_shard_offsets_match_unsharded_bitwise():
+    """The prefill kernel run on one shard (global query offset, keys starting W-1 tokens
+    earlier as the halo, global summaries) reproduces the unsharded run exactly."""
+    from butterfly_b200.seqshard import cuda_ops
+    T, BS, W, world = 8192, 128, 64, 4
+    q, k, v = _inputs(1, 8, 2, T, 128, 21)
+    lay = _layout(T, BS, 2, 4, 6)
+    full = bb.butterfly_compressed_attention(q, k, v, layout=lay, local_window_tokens=W)
+    ks = bb.block_mean_summaries(k, seq_len=T, block_size=BS, num_blocks=T // BS)
+    vs = bb.block_mean_summaries(v, seq_len=T, block_size=BS, num_blocks=T // BS)
+    ops = cuda_ops(lay, W)
+    Tl, h = T // world, W - 1
+    for r in range(world):
+        kv0 = 0 if r == 0 else r * Tl - h
+        y = ops.attend(q[:, :, r * Tl:(r + 1) * Tl], k[:, :, kv0:(r + 1) * Tl], v[:, :, kv0:(r + 1) * Tl],
+                       ks, vs, r * Tl, kv0, T)
+        torch.cuda.synchronize()
+        assert torch.equal(y, full[:, :, r * Tl:(r + 1) * Tl]), r
