@@ -269,7 +269,7 @@ static int check_active_common(const bna_tensor4* q, const bna_tensor4* k, const
   if (Hkv <= 0 || Hq % Hkv != 0 || Hq / Hkv > 16) return fail(BNA_BAD_SHAPE, "bad GQA head counts");
   if (out->size[0] != B || out->size[1] != Hq || out->size[2] != q->size[2]) return fail(BNA_BAD_SHAPE, "out shape mismatch");
   if (window <= 0) return fail(BNA_BAD_SHAPE, "local_window_tokens must be positive");
-  if (window > 1024) return fail(BNA_UNSUPPORTED, "local window above 1024 tokens");
+  if (window > 128) return fail(BNA_UNSUPPORTED, "decode kernel supports local windows up to 128 tokens");
   return BNA_OK;
 }
 

@@ -47,11 +47,13 @@ __device__ __forceinline__ void block_mean(const View4& src, int b, int h, int64
   float acc[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  // cache index of first_pos (one modulo); rows step from it with a wrap
+  const int64_t idx0 = ring > 0 ? first_pos % ring : first_pos - pos_base;
   if (tl < lanes) {
 #pragma unroll 8
     for (int j = tl; j < count; j += lanes) {
-      const int64_t pos = first_pos + j;
-      const int64_t idx = ring > 0 ? pos % ring : pos - pos_base;
+      int64_t idx = idx0 + j;
+      if (ring > 0 && idx >= ring) idx -= ring;
       const uint4 u = ld_nc_128(row_ptr(src, b, h, idx) + ch * 16);
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -121,11 +123,13 @@ __global__ void __launch_bounds__(128) append_kernel(const AppendArgs a) {
 }
 
 // ------------------------------------------------------------------------------ active / decode
-// One CTA (128 threads, 4 warps) per (query index, b * Hkv): stages the query's raw window
-// and routed summaries in shared memory, then each warp computes one query head's scores
-// (lane per key), a warp-shuffle softmax (exp2 domain) and the weighted sum of values
-// (lane per 4 head_dim columns).  Optionally first appends the new token to the ring and
-// closes one block into the summary pool (fused decode step).
+// One CTA (256 threads, 8 warps) per (query index, b * Hkv) serves the G query heads of a
+// KV head.  Keys are spread over the warps for both products: warp w takes keys
+// w, w+8, ...; each lane holds 4 head_dim columns (8-byte coalesced row loads straight
+// from the cache, q of all G heads in registers), scores are warp-shuffle reduced, one
+// warp per head does the softmax (exp2 domain), and the 8 warps' partial outputs are
+// summed through shared memory.  Optionally the CTA first appends the new token to the
+// ring and closes one block into the summary pool (fused decode step).
 struct ActiveArgs {
   int B, Hq, Hkv, G, Tq, dh, window;
   float scale_log2;
@@ -141,135 +145,184 @@ struct ActiveArgs {
   const void* vnew;
   int64_t kn_b, kn_h, vn_b, vn_h;
   int64_t close_block, close_slot;
+  // routed summaries precomputed on the host (decode step: one known position); -1: on device
+  int host_ns;
+  int host_ids[kMaxSummaries];
 };
 
-constexpr int kRowPad = 16;  // bytes of padding per staged row (bank spread)
+constexpr int kDecodeThreads = 256;
+constexpr int kDecodeWarps = kDecodeThreads / 32;
 
-template <typename T>
-__global__ void __launch_bounds__(128) active_kernel(const ActiveArgs a) {
-  extern __shared__ uint8_t smem[];
-  const int dh = a.dh;  // 128
-  const int rowb = dh * 2 + kRowPad;
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+               "l"(gsrc)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+template <typename T, int G>
+__global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const ActiveArgs a) {
+  extern __shared__ __align__(16) uint8_t dsm_raw[];
   const int maxk = a.window + kMaxSummaries;
-  uint8_t* sk = smem;
-  uint8_t* sv = sk + maxk * rowb;
-  float* sq = reinterpret_cast<float*>(sv + maxk * rowb);  // [G][dh]
-  float* sp = sq + a.G * dh;                              // [G][maxk]
-  float* red = sp + a.G * maxk;                           // [128 * 8] for block means
+  constexpr int kRow = 256 + 16;                                   // padded staged row (bank spread)
+  uint8_t* kv = dsm_raw;                                           // [2][maxk][kRow] K rows, V rows
+  float* sc = reinterpret_cast<float*>(kv + 2 * maxk * kRow);      // [G][maxk] scores -> weights
+  float* qs = sc + G * maxk;                                       // [G][128] scaled queries
+  float* red = qs + G * 128;                                       // [256 * 8] block-mean reduction
+  constexpr int kRed = kDecodeThreads * 8 > 512 * G ? kDecodeThreads * 8 : 512 * G;
+  float* stat = red + kRed;                                        // [G] row sums
+  int* sel = reinterpret_cast<int*>(stat + G);                     // [1 + 16] summary count + ids
 
   const int t = blockIdx.x;
   const int b = blockIdx.y / a.Hkv, kvh = blockIdx.y % a.Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t p = a.positions ? a.positions[t] : a.pos0 + t;
-  const int chunks = dh >> 3;
 
-  if (a.knew) {  // fused append of the new token at position p
-    const int64_t slot = p % a.ring;
-    for (int c = threadIdx.x; c < 2 * chunks; c += blockDim.x) {
-      const bool isv = c >= chunks;
-      const int ch = isv ? c - chunks : c;
-      const uint8_t* src = reinterpret_cast<const uint8_t*>(isv ? a.vnew : a.knew) +
-                           2 * (b * (isv ? a.vn_b : a.kn_b) + kvh * (isv ? a.vn_h : a.kn_h));
-      st_128(row_ptr(isv ? a.v : a.k, b, kvh, slot) + ch * 16, ld_nc_128(src + ch * 16));
-    }
-  }
-  if (a.close_block >= 0) {  // fused block close: mean of the block's tokens from the ring
-    const int BS = a.route.block_size;
-    block_mean<T>(a.k, b, kvh, a.close_block * BS, BS, 0, a.ring, dh, red, row_ptr(a.ks, b, kvh, a.close_slot));
-    __syncthreads();
-    block_mean<T>(a.v, b, kvh, a.close_block * BS, BS, 0, a.ring, dh, red, row_ptr(a.vs, b, kvh, a.close_slot));
-  }
-  __syncthreads();
-
-  // raw window [lo, hi] and routed summaries
+  // raw window [lo, hi]; with a fused append the newest row (p) is read from the input
   int64_t lo = max64(0, p - a.window + 1);
   if (a.ring == 0) lo = max64(lo, a.kv_pos0);
   int64_t hi = p;
   if (hi > a.kv_len - 1) hi = a.kv_len - 1;
   const int nraw = hi >= lo ? (int)(hi - lo + 1) : 0;
-  int ids[kMaxSummaries];
-  const int ns = active_summaries(a.route, p, a.window, a.num_summary_limit, a.route.neighbors, ids);
-  const int nk = nraw + ns;
-  for (int c = threadIdx.x; c < nk * chunks; c += blockDim.x) {
-    const int r = c / chunks, ch = c % chunks;
-    uint4 ku, vu;
-    if (r < nraw) {
-      const int64_t pos = lo + r;
-      const int64_t idx = a.ring > 0 ? pos % a.ring : pos - a.kv_pos0;
-      ku = ld_128(row_ptr(a.k, b, kvh, idx) + ch * 16);
-      vu = ld_128(row_ptr(a.v, b, kvh, idx) + ch * 16);
+  const int ring = (int)a.ring;
+  const int idx_lo = ring > 0 ? (int)((uint64_t)lo % (uint64_t)a.ring) : (int)(lo - a.kv_pos0);
+#pragma unroll 1
+  for (int c = threadIdx.x; c < 2 * nraw * 16; c += kDecodeThreads) {
+    const int isv = c >= nraw * 16;
+    const int e = isv ? c - nraw * 16 : c;
+    const int j = e >> 4, ch = e & 15;
+    const uint8_t* src;
+    if (a.knew && j == nraw - 1) {
+      src = reinterpret_cast<const uint8_t*>(isv ? a.vnew : a.knew) +
+            2 * (b * (isv ? a.vn_b : a.kn_b) + kvh * (isv ? a.vn_h : a.kn_h));
     } else {
-      ku = ld_128(row_ptr(a.ks, b, kvh, ids[r - nraw]) + ch * 16);
-      vu = ld_128(row_ptr(a.vs, b, kvh, ids[r - nraw]) + ch * 16);
+      int idx = idx_lo + j;
+      if (ring > 0 && idx >= ring) idx -= ring;
+      src = row_ptr(isv ? a.v : a.k, b, kvh, idx);
     }
-    *reinterpret_cast<uint4*>(sk + r * rowb + ch * 16) = ku;
-    *reinterpret_cast<uint4*>(sv + r * rowb + ch * 16) = vu;
+    cp_async_16(kv + (isv * maxk + j) * kRow + ch * 16, src + ch * 16);
   }
-  for (int c = threadIdx.x; c < a.G * chunks; c += blockDim.x) {
-    const int g = c / chunks, ch = c % chunks;
-    const uint4 u = ld_nc_128(row_ptr(a.q, b, kvh * a.G + g, t) + ch * 16);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = ElemTraits<T>::unpack2(w[e]);
-      sq[g * dh + ch * 8 + 2 * e] = f.x * a.scale_log2;
-      sq[g * dh + ch * 8 + 2 * e + 1] = f.y * a.scale_log2;
-    }
+  if (a.knew && threadIdx.x < 32) {  // fused append of the new token into ring slot p % ring
+    const int slot = (int)((uint64_t)p % (uint64_t)a.ring);
+    const bool isv = threadIdx.x >= 16;
+    const int ch = threadIdx.x & 15;
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(isv ? a.vnew : a.knew) +
+                         2 * (b * (isv ? a.vn_b : a.kn_b) + kvh * (isv ? a.vn_h : a.kn_h));
+    st_128(row_ptr(isv ? a.v : a.k, b, kvh, slot) + ch * 16, ld_nc_128(src + ch * 16));
+  }
+#pragma unroll 1
+  for (int c = threadIdx.x; c < G * 64; c += kDecodeThreads) {  // queries, scaled to log2 units
+    const int g = c >> 6, d = (c & 63) * 2;
+    const float2 f = ElemTraits<T>::unpack2(*reinterpret_cast<const uint32_t*>(row_ptr(a.q, b, kvh * G + g, t) + d * 2));
+    qs[g * 128 + d] = f.x * a.scale_log2;
+    qs[g * 128 + d + 1] = f.y * a.scale_log2;
+  }
+  if (a.close_block >= 0) {  // fused block close: mean of the block's tokens from the ring
+    const int BS = a.route.block_size;
+    block_mean<T>(a.k, b, kvh, a.close_block * BS, BS, 0, a.ring, 128, red, row_ptr(a.ks, b, kvh, a.close_slot));
+    __syncthreads();
+    block_mean<T>(a.v, b, kvh, a.close_block * BS, BS, 0, a.ring, 128, red, row_ptr(a.vs, b, kvh, a.close_slot));
+    __syncthreads();  // the closed block may be routed to below
+  }
+  if (a.host_ns >= 0) {
+    if (threadIdx.x <= kMaxSummaries) sel[threadIdx.x] = threadIdx.x == 0 ? a.host_ns : a.host_ids[threadIdx.x - 1];
+  } else if (threadIdx.x == 0) {
+    int ids[kMaxSummaries];
+    const int n = active_summaries(a.route, p, a.window, a.num_summary_limit, a.route.neighbors, ids);
+    sel[0] = n;
+    for (int i = 0; i < n; ++i) sel[1 + i] = ids[i];
   }
   __syncthreads();
+  const int ns = sel[0];
+  const int nk = nraw + ns;
+#pragma unroll 1
+  for (int c = threadIdx.x; c < 2 * ns * 16; c += kDecodeThreads) {
+    const int isv = c >= ns * 16;
+    const int e = isv ? c - ns * 16 : c;
+    const int j = e >> 4, ch = e & 15;
+    cp_async_16(kv + (isv * maxk + nraw + j) * kRow + ch * 16,
+                row_ptr(isv ? a.vs : a.ks, b, kvh, sel[1 + j]) + ch * 16);
+  }
+  cp_async_wait_all();
+  __syncthreads();
 
-  const int nwarps = blockDim.x >> 5;
-  for (int g = warp; g < a.G; g += nwarps) {
-    const float* qv = sq + g * dh;
-    float* pr = sp + g * maxk;
-    float m = -INFINITY;
-    for (int j = lane; j < nk; j += 32) {
-      const uint8_t* kr = sk + j * rowb;
-      float s = 0.f;
-      for (int ch = 0; ch < chunks; ++ch) {
-        const uint4 u = *reinterpret_cast<const uint4*>(kr + ch * 16);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = ElemTraits<T>::unpack2(w[e]);
-          s = fmaf(qv[ch * 8 + 2 * e], f.x, s);
-          s = fmaf(qv[ch * 8 + 2 * e + 1], f.y, s);
-        }
-      }
-      pr[j] = s;
-      m = fmaxf(m, s);
+  // scores: one thread per (key, head), full 128-wide dot from shared memory
+#pragma unroll 1
+  for (int e = threadIdx.x; e < nk * G; e += kDecodeThreads) {
+    const int j = e / G, g = e - j * G;
+    const uint4* kr = reinterpret_cast<const uint4*>(kv + j * kRow);
+    const float4* q4 = reinterpret_cast<const float4*>(qs + g * 128);
+    float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll 4
+    for (int c = 0; c < 16; ++c) {
+      const uint4 u = kr[c];
+      const float4 qa = q4[2 * c], qb = q4[2 * c + 1];
+      const float2 f0 = ElemTraits<T>::unpack2(u.x), f1 = ElemTraits<T>::unpack2(u.y);
+      const float2 f2 = ElemTraits<T>::unpack2(u.z), f3 = ElemTraits<T>::unpack2(u.w);
+      d0 = fmaf(qa.x, f0.x, fmaf(qa.y, f0.y, d0));
+      d1 = fmaf(qa.z, f1.x, fmaf(qa.w, f1.y, d1));
+      d2 = fmaf(qb.x, f2.x, fmaf(qb.y, f2.y, d2));
+      d3 = fmaf(qb.z, f3.x, fmaf(qb.w, f3.y, d3));
     }
+    sc[g * maxk + j] = (d0 + d1) + (d2 + d3);
+  }
+  __syncthreads();
+  // softmax: warp g (looping if G > warps) owns head g; weights overwrite the scores
+#pragma unroll 1
+  for (int g = warp; g < G; g += kDecodeWarps) {
+    float* sg = sc + g * maxk;
+    float m = -INFINITY;
+    for (int j = lane; j < nk; j += 32) m = fmaxf(m, sg[j]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float l = 0.f;
     for (int j = lane; j < nk; j += 32) {
-      const float e = exp2f(pr[j] - m);
-      pr[j] = e;
+      const float e = exp2f(sg[j] - m);
+      sg[j] = e;
       l += e;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    __syncwarp();
-    // lane owns head_dim columns [4*lane, 4*lane + 4)
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < nk; ++j) {
-      const float w = pr[j];
-      const uint2 u = *reinterpret_cast<const uint2*>(sv + j * rowb + lane * 8);
-      const float2 f0 = ElemTraits<T>::unpack2(u.x), f1 = ElemTraits<T>::unpack2(u.y);
-      acc[0] = fmaf(w, f0.x, acc[0]);
-      acc[1] = fmaf(w, f0.y, acc[1]);
-      acc[2] = fmaf(w, f1.x, acc[2]);
-      acc[3] = fmaf(w, f1.y, acc[3]);
+    if (lane == 0) {
+      stat[g] = l;
+      if (a.lse) a.lse[b * a.ls_b + (int64_t)(kvh * G + g) * a.ls_h + t] = (m + log2f(l)) * 0.6931471805599453f;
     }
+  }
+  __syncthreads();
+  // weighted values: thread = (key quarter, head, 2 columns); the 4 key quarters' partial
+  // sums meet in shared memory (reusing the block-mean buffer)
+  float* part = red;  // [4][G * 64][2]
+  const int npairs = G * 64;
+#pragma unroll 1
+  for (int e = threadIdx.x; e < 4 * npairs; e += kDecodeThreads) {
+    const int qtr = e / npairs, r = e - qtr * npairs;
+    const int g = r >> 6, c = (r & 63) * 2;
+    const float* w = sc + g * maxk;
+    const uint8_t* vb = kv + maxk * kRow + c * 2;
+    const int j0 = (nk * qtr) >> 2, j1 = (nk * (qtr + 1)) >> 2;
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll 2
+    for (int j = j0; j < j1; ++j) {
+      const float2 f = ElemTraits<T>::unpack2(*reinterpret_cast<const uint32_t*>(vb + j * kRow));
+      s0 = fmaf(w[j], f.x, s0);
+      s1 = fmaf(w[j], f.y, s1);
+    }
+    *reinterpret_cast<float2*>(part + 2 * (qtr * npairs + r)) = make_float2(s0, s1);
+  }
+  __syncthreads();
+#pragma unroll 1
+  for (int r = threadIdx.x; r < npairs; r += kDecodeThreads) {
+    const int g = r >> 6, c = (r & 63) * 2;
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int qtr = 0; qtr < 4; ++qtr) {
+      const float2 f = *reinterpret_cast<const float2*>(part + 2 * (qtr * npairs + r));
+      s0 += f.x;
+      s1 += f.y;
+    }
+    const float l = stat[g];
     const float inv = l > 0.f ? 1.f / l : 0.f;
-    uint8_t* orow = row_ptr(a.out, b, kvh * a.G + g, t);
-    uint2 o;
-    o.x = ElemTraits<T>::pack2(acc[0] * inv, acc[1] * inv);
-    o.y = ElemTraits<T>::pack2(acc[2] * inv, acc[3] * inv);
-    *reinterpret_cast<uint2*>(orow + lane * 8) = o;
-    if (a.lse && lane == 0)
-      a.lse[b * a.ls_b + (int64_t)(kvh * a.G + g) * a.ls_h + t] = (m + log2f(l)) * 0.6931471805599453f;
-    __syncwarp();
+    *reinterpret_cast<uint32_t*>(row_ptr(a.out, b, kvh * G + g, t) + c * 2) = ElemTraits<T>::pack2(s0 * inv, s1 * inv);
   }
 }
 
@@ -311,6 +364,11 @@ int launch_active(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4*
                   int64_t ring, int64_t kv_len, int num_summary_limit, float scale, const bna_tensor4* knew,
                   const bna_tensor4* vnew, int64_t close_block, int64_t close_slot, cudaStream_t stream) {
   ActiveArgs a{};
+  a.host_ns = -1;
+  if (!positions && q->size[2] == 1 && route->neighbors == nullptr) {
+    // one query at a known position: route it here (same selection code as the device)
+    a.host_ns = active_summaries(*route, pos0, window, num_summary_limit, nullptr, a.host_ids);
+  }
   a.B = (int)q->size[0];
   a.Hq = (int)q->size[1];
   a.Tq = (int)q->size[2];
@@ -346,19 +404,27 @@ int launch_active(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4*
   a.close_block = close_block;
   a.close_slot = close_slot;
   const int maxk = window + kMaxSummaries;
-  const size_t smem = (size_t)2 * maxk * (a.dh * 2 + kRowPad) + sizeof(float) * ((size_t)a.G * a.dh + (size_t)a.G * maxk + 128 * 8);
+  const size_t smem = (size_t)2 * maxk * (256 + 16) +
+                      sizeof(float) * ((size_t)a.G * maxk + (size_t)a.G * 128 +
+                                       (size_t)(kDecodeThreads * 8 > 512 * a.G ? kDecodeThreads * 8 : 512 * a.G) +
+                                       (size_t)a.G) +
+                      sizeof(int) * (1 + kMaxSummaries);
   dim3 grid((unsigned)a.Tq, (unsigned)(a.B * a.Hkv));
   if (grid.x == 0 || grid.y == 0) return BNA_OK;
-  if (dtype == BNA_BF16) {
-    auto kern = active_kernel<__nv_bfloat16>;
+  auto launch = [&](auto kern) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<grid, 128, smem, stream>>>(a);
-  } else {
-    auto kern = active_kernel<__half>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<grid, 128, smem, stream>>>(a);
+    kern<<<grid, kDecodeThreads, smem, stream>>>(a);
+  };
+  const bool bf = dtype == BNA_BF16;
+  switch (a.G) {
+    case 1: bf ? launch(decode_kernel<__nv_bfloat16, 1>) : launch(decode_kernel<__half, 1>); break;
+    case 2: bf ? launch(decode_kernel<__nv_bfloat16, 2>) : launch(decode_kernel<__half, 2>); break;
+    case 4: bf ? launch(decode_kernel<__nv_bfloat16, 4>) : launch(decode_kernel<__half, 4>); break;
+    case 8: bf ? launch(decode_kernel<__nv_bfloat16, 8>) : launch(decode_kernel<__half, 8>); break;
+    case 16: bf ? launch(decode_kernel<__nv_bfloat16, 16>) : launch(decode_kernel<__half, 16>); break;
+    default: return fail(BNA_UNSUPPORTED, "GQA group size must be 1, 2, 4, 8 or 16");
   }
-  return check_cuda(cudaGetLastError(), "active_kernel launch");
+  return check_cuda(cudaGetLastError(), "decode_kernel launch");
 }
 
 int launch_selection_dump(const bna_route* r, int window, int32_t* idx, int32_t* cnt, cudaStream_t stream) {

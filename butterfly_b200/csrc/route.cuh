@@ -119,7 +119,9 @@ BNA_HD int prefill_summaries(const bna_route& r, int b, int window, const int32_
 
 // Active row at position p: block = min(p / BS, N - 1); cutoff = max(0, p - W + 1) (:996-997).
 BNA_HD int active_block(const bna_route& r, int64_t p) {
-  int64_t blk = p / (r.block_size > 0 ? r.block_size : 1);
+  // positions below 2^31 (always, in practice) take the 32-bit division
+  const int bs = r.block_size > 0 ? r.block_size : 1;
+  int64_t blk = (p >= 0 && p < 0x7FFFFFFF) ? (int64_t)((int)p / bs) : p / bs;
   if (blk < 0) blk = 0;
   if (blk > r.num_blocks - 1) blk = r.num_blocks - 1;
   return (int)(blk < 0 ? 0 : blk);
