@@ -160,7 +160,7 @@ def compress_bytes_per_pair() -> int:
 
 
 def run_prefill(dev, seed, steps, warmup, sampler):
-    from butterfly_b200.attention import block_mean_summaries, prefill_attention_into, route_for
+    from butterfly_b200.attention import block_mean_summaries_kv, prefill_attention_into, route_for
     g = torch.Generator(device=dev).manual_seed(seed)
     ins = []
     for _ in LAYERS:
@@ -182,8 +182,7 @@ def run_prefill(dev, seed, steps, warmup, sampler):
             q, k, v = ins[i]
             if si is not None:
                 ev[si][i][0].record()
-            block_mean_summaries(k, seq_len=T, block_size=BS, num_blocks=N, out=ks[i])
-            block_mean_summaries(v, seq_len=T, block_size=BS, num_blocks=N, out=vs[i])
+            block_mean_summaries_kv(k, v, seq_len=T, block_size=BS, num_blocks=N, k_out=ks[i], v_out=vs[i])
             if si is not None:
                 ev[si][i][1].record()
             prefill_attention_into(q, k, v, ks[i], vs[i], outs[i], None, routes[i], W, scale)
@@ -369,8 +368,8 @@ def prefill_trace(dev):
     _lib.lib().bna_set_prefill_trace(None)
     tr = buf.view(nsm, 64, 16).cpu().numpy().astype("int64")
     t0 = tr[:, :, :16][tr[:, :, :16] > 0].min()
-    names = ["prod_start", "v_landed", "prod_full", "mma_qk", "mma_pv", "smx_s", "smx_p", "smx_o", "smx_done",
-             "smx_ld", "smx_max", "smx_st_issued", "qk_landed", "smx_meta", "v_start", "v_full"]
+    names = ["q_issued", "k_dep_ok", "prod_full", "mma_qk", "mma_pv", "smx_s", "smx_p", "smx_o", "smx_done",
+             "route_begin", "route_end", "k_tma_issued", "cpasync_issued", "smx_meta", "v_start", "v_full"]
     for cta in (0,):
         print(f"cta {cta} (us from kernel start)")
         for i in range(16):
@@ -505,7 +504,7 @@ def main():
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_val, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "butterfly_b200.butterfly_compressed_attention from pinned host buffers"},
-        "gpu_launches": args.steps * len(LAYERS) * 3,
+        "gpu_launches": args.steps * len(LAYERS) * 2,
         "clocks": clocks,
         "decode": decode,
     }

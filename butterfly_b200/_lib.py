@@ -20,7 +20,7 @@ RULES = {"causal_shift": 0, "xor": 1, "bit_reversal": 2, "benes": 3}
 EXPORTED = (
     "bna_last_error", "bna_version", "bna_take_device_error", "bna_set_prefill_trace", "bna_route_init",
     "bna_block_neighbors_host", "bna_prefill_selection_host", "bna_active_selection_host",
-    "bna_prefill_selection_device", "bna_compress_blocks", "bna_prefill_attention",
+    "bna_prefill_selection_device", "bna_compress_blocks", "bna_compress_kv_blocks", "bna_prefill_attention",
     "bna_active_attention", "bna_cache_append", "bna_decode_step", "bna_prefill_attention_static_scratch",
 )
 
@@ -66,6 +66,7 @@ def lib() -> ctypes.CDLL:
             "bna_active_selection_host": (i32, [R, i32, P64, i32, i32, P32, P32, P32, P32]),
             "bna_prefill_selection_device": (i32, [R, i32, i32, vp, vp, vp]),
             "bna_compress_blocks": (i32, [T4, T4, i32, i32, i64, i32, i64, i64, i64, vp]),
+            "bna_compress_kv_blocks": (i32, [T4, T4, T4, T4, i32, i32, i64, i32, i64, i64, i64, vp]),
             "bna_prefill_attention": (i32, [T4, T4, T4, T4, T4, T4, vp, i64, i64, i32, R, i32, i64, i64, i64, f32, vp]),
             "bna_active_attention": (i32, [T4, T4, T4, T4, T4, T4, vp, i64, i64, i32, R, i32, vp, i64, i64, i64, i32, f32, vp]),
             "bna_cache_append": (i32, [T4, T4, T4, T4, i32, i64, i64, vp]),

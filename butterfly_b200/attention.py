@@ -70,6 +70,24 @@ def block_mean_summaries(x: torch.Tensor, *, seq_len: int, block_size: int, num_
     return out
 
 
+def block_mean_summaries_kv(k: torch.Tensor, v: torch.Tensor, *, seq_len: int, block_size: int, num_blocks: int,
+                            k_out: Optional[torch.Tensor] = None, v_out: Optional[torch.Tensor] = None):
+    """Block means of K and V in one launch: two [B,H,T,dh] -> two [B,H,N,dh]."""
+    B, H, T, dh = k.shape
+    if int(T) != int(seq_len) or tuple(v.shape) != tuple(k.shape):
+        raise ValueError(f"summary seq_len mismatch: k/v have shapes {tuple(k.shape)}/{tuple(v.shape)}, T={seq_len}")
+    _lib.require_cuda(k, v)
+    if k_out is None:
+        k_out = torch.empty((B, H, int(num_blocks), dh), device=k.device, dtype=k.dtype)
+    if v_out is None:
+        v_out = torch.empty_like(k_out)
+    tk, tv, tko, tvo = (_lib.t4(x) for x in (k, v, k_out, v_out))
+    _lib.check(_lib.lib().bna_compress_kv_blocks(
+        ctypes.byref(tk), ctypes.byref(tv), ctypes.byref(tko), ctypes.byref(tvo), _lib.dtype_code(k.dtype),
+        int(block_size), 0, int(num_blocks), int(seq_len), 0, 0, _lib.stream_ptr(k.device)))
+    return k_out, v_out
+
+
 def _lse_args(lse: Optional[torch.Tensor]):
     if lse is None:
         return None, 0, 0
@@ -115,8 +133,11 @@ def butterfly_compressed_attention(
     if N != -(-int(T) // BS):
         raise ValueError(f"layout has {N} blocks but T={T} needs {-(-int(T) // BS)}")
     route, _keep = route_for(layout, q.device)
-    ks = block_mean_summaries(k, seq_len=T, block_size=BS, num_blocks=N)
-    vs = block_mean_summaries(v, seq_len=T, block_size=BS, num_blocks=N)
+    if tuple(k.shape) == tuple(v.shape):
+        ks, vs = block_mean_summaries_kv(k, v, seq_len=T, block_size=BS, num_blocks=N)
+    else:
+        ks = block_mean_summaries(k, seq_len=T, block_size=BS, num_blocks=N)
+        vs = block_mean_summaries(v, seq_len=T, block_size=BS, num_blocks=N)
     out = torch.empty((batch, T, H_q, dh), device=q.device, dtype=q.dtype).transpose(1, 2)
     lse = torch.empty((batch, H_q, T), device=q.device, dtype=torch.float32) if return_lse else None
     sc = float(scale) if scale is not None else 1.0 / math.sqrt(dh)

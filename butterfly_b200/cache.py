@@ -97,11 +97,11 @@ class CompressedKVCache:
         assert blocks == list(range(first, first + len(blocks)))
         dev = self._tail_k.device
         dt = _lib.dtype_code(self._tail_k.dtype)
-        for src, dst in ((self._tail_k, self._sum_k), (self._tail_v, self._sum_v)):
-            ts, td = _lib.t4(src), _lib.t4(dst)
-            _lib.check(_lib.lib().bna_compress_blocks(
-                ctypes.byref(ts), ctypes.byref(td), dt, self.block_size, first * self.block_size, len(blocks),
-                len(blocks) * self.block_size, self.ring, self.summary_count, _lib.stream_ptr(dev)))
+        tk, tv, sk, sv = (_lib.t4(x) for x in (self._tail_k, self._tail_v, self._sum_k, self._sum_v))
+        _lib.check(_lib.lib().bna_compress_kv_blocks(
+            ctypes.byref(tk), ctypes.byref(tv), ctypes.byref(sk), ctypes.byref(sv), dt, self.block_size,
+            first * self.block_size, len(blocks), len(blocks) * self.block_size, self.ring, self.summary_count,
+            _lib.stream_ptr(dev)))
         self.summary_count += len(blocks)
         self.summary_offset += len(blocks) * self.block_size
 

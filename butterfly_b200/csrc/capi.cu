@@ -27,7 +27,7 @@ int launch_prefill(const bna_tensor4*, const bna_tensor4*, const bna_tensor4*, c
                    const bna_tensor4*, bna_tensor4*, float*, int64_t, int64_t, int, const bna_route*, int,
                    int64_t, int64_t, int64_t, float, cudaStream_t);
 int launch_compress(const bna_tensor4*, bna_tensor4*, int, int, int64_t, int, int64_t, int64_t, int64_t,
-                    cudaStream_t);
+                    cudaStream_t, const bna_tensor4*, bna_tensor4*);
 int launch_append(bna_tensor4*, bna_tensor4*, const bna_tensor4*, const bna_tensor4*, int64_t, int64_t,
                   cudaStream_t);
 int launch_active(const bna_tensor4*, const bna_tensor4*, const bna_tensor4*, const bna_tensor4*,
@@ -191,8 +191,8 @@ int bna_prefill_selection_device(const bna_route* r, int32_t seq_len, int32_t wi
   return launch_selection_dump(r, window, summary_idx, summary_count, (cudaStream_t)stream);
 }
 
-int bna_compress_blocks(const bna_tensor4* x, bna_tensor4* out, int32_t dtype, int32_t block_size, int64_t pos0,
-                        int32_t n_blocks, int64_t valid_len, int64_t ring, int64_t slot0, void* stream) {
+static int check_compress(const bna_tensor4* x, bna_tensor4* out, int32_t dtype, int32_t block_size, int32_t n_blocks,
+                          int64_t valid_len, int64_t ring, int64_t slot0) {
   if (int rc = check_dtype(dtype)) return rc;
   if (null4(x) || null4(out)) return fail(BNA_BAD_SHAPE, "null tensor");
   const int64_t dh = x->size[3];
@@ -207,7 +207,25 @@ int bna_compress_blocks(const bna_tensor4* x, bna_tensor4* out, int32_t dtype, i
   if (ring == 0 && valid_len > x->size[2]) return fail(BNA_BAD_SHAPE, "valid_len exceeds x's length");
   if (ring > 0 && ring > x->size[2]) return fail(BNA_BAD_SHAPE, "ring exceeds x's length");
   if (ring == 0 && (int64_t)n_blocks * block_size < valid_len) return fail(BNA_BAD_SHAPE, "n_blocks do not cover valid_len");
-  return launch_compress(x, out, dtype, block_size, pos0, n_blocks, valid_len, ring, slot0, (cudaStream_t)stream);
+  return BNA_OK;
+}
+
+int bna_compress_blocks(const bna_tensor4* x, bna_tensor4* out, int32_t dtype, int32_t block_size, int64_t pos0,
+                        int32_t n_blocks, int64_t valid_len, int64_t ring, int64_t slot0, void* stream) {
+  if (int rc = check_compress(x, out, dtype, block_size, n_blocks, valid_len, ring, slot0)) return rc;
+  return launch_compress(x, out, dtype, block_size, pos0, n_blocks, valid_len, ring, slot0, (cudaStream_t)stream,
+                         nullptr, nullptr);
+}
+
+int bna_compress_kv_blocks(const bna_tensor4* k, const bna_tensor4* v, bna_tensor4* k_out, bna_tensor4* v_out,
+                           int32_t dtype, int32_t block_size, int64_t pos0, int32_t n_blocks, int64_t valid_len,
+                           int64_t ring, int64_t slot0, void* stream) {
+  if (int rc = check_compress(k, k_out, dtype, block_size, n_blocks, valid_len, ring, slot0)) return rc;
+  if (int rc = check_compress(v, v_out, dtype, block_size, n_blocks, valid_len, ring, slot0)) return rc;
+  for (int i = 0; i < 4; ++i)
+    if (k->size[i] != v->size[i] || k_out->size[i] != v_out->size[i]) return fail(BNA_BAD_SHAPE, "k and v shapes differ");
+  return launch_compress(k, k_out, dtype, block_size, pos0, n_blocks, valid_len, ring, slot0, (cudaStream_t)stream,
+                         v, v_out);
 }
 
 int bna_prefill_attention(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4* v,

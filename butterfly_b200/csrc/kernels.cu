@@ -81,7 +81,7 @@ __device__ __forceinline__ void block_mean(const View4& src, int b, int h, int64
 }
 
 struct CompressArgs {
-  View4 src, dst;
+  View4 src, dst, src2, dst2;  // src2/dst2: second tensor of a K/V pair (blockIdx.z == 1)
   int H, dh, block_size;
   int64_t pos0, valid_len, ring, slot0;
 };
@@ -99,7 +99,9 @@ __global__ void __launch_bounds__(kCompressThreads) compress_kernel(const Compre
   int64_t cnt = a.valid_len - (int64_t)j * a.block_size;
   if (cnt > a.block_size) cnt = a.block_size;
   if (cnt < 1) cnt = 0;
-  block_mean<T>(a.src, b, h, first, (int)cnt, a.pos0, a.ring, a.dh, red, row_ptr(a.dst, b, h, a.slot0 + j));
+  const bool second = blockIdx.z == 1;
+  block_mean<T>(second ? a.src2 : a.src, b, h, first, (int)cnt, a.pos0, a.ring, a.dh, red,
+                row_ptr(second ? a.dst2 : a.dst, b, h, a.slot0 + j));
 }
 
 // ------------------------------------------------------------------------------ cache append
@@ -338,9 +340,11 @@ __global__ void prefill_selection_kernel(const bna_route r, int window, int32_t*
 
 // ------------------------------------------------------------------------------ launchers
 int launch_compress(const bna_tensor4* x, bna_tensor4* out, int dtype, int block_size, int64_t pos0,
-                    int n_blocks, int64_t valid_len, int64_t ring, int64_t slot0, cudaStream_t stream) {
-  CompressArgs a{to_view(x), to_view(out), (int)x->size[1], (int)x->size[3], block_size, pos0, valid_len, ring, slot0};
-  dim3 grid(n_blocks, (unsigned)(x->size[0] * x->size[1]));
+                    int n_blocks, int64_t valid_len, int64_t ring, int64_t slot0, cudaStream_t stream,
+                    const bna_tensor4* x2, bna_tensor4* out2) {
+  CompressArgs a{to_view(x), to_view(out), to_view(x2 ? x2 : x), to_view(out2 ? out2 : out), (int)x->size[1],
+                 (int)x->size[3], block_size, pos0, valid_len, ring, slot0};
+  dim3 grid(n_blocks, (unsigned)(x->size[0] * x->size[1]), x2 ? 2u : 1u);
   if (n_blocks == 0 || grid.y == 0) return BNA_OK;
   if (dtype == BNA_BF16)
     compress_kernel<__nv_bfloat16><<<grid, kCompressThreads, 0, stream>>>(a);

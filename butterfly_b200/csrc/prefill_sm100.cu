@@ -7,24 +7,26 @@
 // GQA: the G = Hq/Hkv query heads of a KV head share its keys.
 //
 // Work unit = (batch b, KV head, query tile of QT = 128/G positions).  Its 128 MMA rows
-// are the G heads x QT positions (M = 128).  The keys of a unit are one contiguous slice
-// of NR = round_up(W - 1 + QT, 16) raw positions starting at q0 - (W - 1), followed by 16
-// rows holding the block's routed summaries (zero rows where unused), so
-//   S = Q . [K_slice ; K_sum]^T            one tcgen05.mma chain, N = NR + 16, fp32 in TMEM
-//   P = masked softmax(S)                  exp2 domain, fp32 row sums; P stored as 16-bit
-//                                          values back into the S columns of TMEM
-//   O = P . [V_slice ; V_sum]              tcgen05.mma with A = P read from TMEM and V an
-//                                          MN-major shared-memory operand
-// Loads: Q, K, V slices by TMA (128-byte swizzle, zero fill outside the tensor) into a
-// 2-stage ring; the summary rows by the producer warp with 128-bit loads written into the
-// same swizzled tiles.
+// are the G heads x QT positions (M = 128).  The keys of a unit are the NR =
+// round_up(W - 1 + QT, 16) raw positions starting at q0 - (W - 1), then a 16-row tile of
+// the block's routed summaries (zero rows where unused):
+//   S = Q . [K_window ; K_sum]^T     tcgen05.mma chains into TMEM (fp32)
+//   P = masked softmax(S)            exp2 domain, fp32 row sums; P written back as 16-bit
+//                                    values into the S columns of TMEM
+//   O = P . [V_window ; V_sum]       tcgen05.mma with A = P from TMEM, V an MN-major operand
 //
-// Warp roles (320 threads, one CTA per SM, persistent over units):
-//   warp 0       producer: TMA issue + summary rows
-//   warp 1       TMEM allocator + single-thread MMA issuer
-//   warps 2..5   softmax/epilogue group 0 (even local units)
-//   warps 6..9   softmax/epilogue group 1 (odd local units)
-// The two groups ping-pong so one group's softmax overlaps the other's MMAs and loads.
+// Sliding window.  Each CTA processes a contiguous range of units; consecutive units of
+// one (b, KV head) advance by QT positions, so K and V live in shared-memory rings of
+// R = NR + 2 QT rows and a unit loads only its QT new rows (a whole window only when a run
+// of one (b, KV head) starts).  Q streams through a ring of QS tiles.  All loads are TMA
+// (128-byte swizzle, zero fill outside the tensor); summary rows are copied by the producer
+// warps with cp.async whose completion arrives on the same barrier as the TMA bytes.
+//
+// Warp roles (608 threads, one CTA per SM):
+//   warp 0        Q + K producer        warp 18        V producer
+//   warp 1        TMEM allocator + single-thread MMA issuer
+//   warps 2..17   two softmax/epilogue groups of 8 warps (units alternate between them);
+//                 two warps share each TMEM lane quarter and split the columns
 // TMEM (512 columns): group g's S/P tile at [128g, 128g+128), its O tile at 256 + 128g.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -38,7 +40,7 @@ namespace bna {
 
 struct PrefillArgs {
   int B, Hq, Hkv, G, Tq;
-  int QT, NR, ntiles, total_units, stages;
+  int QT, NR, ntiles, total_units, QS;
   int q_tmajor;  // Q tile rows ordered (position, head) instead of (head, position)
   int64_t q_pos0, kv_pos0, total_len;
   int q_pos0_i, kidx0, blk0, tiles_per_block;  // 32-bit forms of the position math
@@ -56,18 +58,20 @@ struct PrefillArgs {
   uint64_t* trace;  // optional timeline: [cta][unit < 64][16] globaltimer stamps
 };
 
+// Shared-memory plan (1024-byte aligned regions).
 struct PrefillSmem {
-  uint32_t q, kv_rows, kv_half, k, v, stage, xchg, bars, total;
-  __host__ __device__ PrefillSmem(int NR, int stages) {
-    q = 0;                              // 2 halves x 128 rows x 128 B
-    kv_rows = (uint32_t)NR + 16;        // raw slice + summary rows
-    kv_half = kv_rows * 128;            // one 64-column half of a K or V tile
-    k = 32768;
-    v = k + 2 * kv_half;
-    stage = v + 2 * kv_half;
-    xchg = stage * stages;      // 4 x 256 floats of row max / sum exchange
+  uint32_t R, q, kring, ring_half, vring, ksum, vsum, xchg, bars, total;
+  __host__ __device__ PrefillSmem(int NR, int QT, int QS) {
+    R = (uint32_t)(NR + 2 * QT);        // ring rows (multiple of 16)
+    q = 0;                              // QS tiles x 2 halves x 128 rows x 128 B
+    ring_half = R * 128;                // one 64-column half of a ring
+    kring = (uint32_t)QS * 32768;
+    vring = kring + 2 * ring_half;
+    ksum = vring + 2 * ring_half;       // 3 slots x 2 halves x 16 rows x 128 B
+    vsum = ksum + 3 * 4096;
+    xchg = vsum + 3 * 4096;             // [2 groups][2 buffers][2 halves][128] row maxima
     bars = xchg + 4096;
-    total = bars + 256 + 1024;  // + alignment slack
+    total = bars + 512 + 1024;          // + alignment slack
   }
 };
 
@@ -75,7 +79,7 @@ namespace {
 
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kThreads = 608;  // 19 warps
-constexpr int kVWarp = 18;    // producer of the V part of each stage
+constexpr int kVWarp = 18;     // V producer
 
 template <typename T, int NR_>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -84,32 +88,37 @@ __global__ void __launch_bounds__(kThreads, 1)
   using namespace sm100;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const PrefillSmem L(a.NR, a.stages);
+  const int QT = a.QT, G = a.G, QS = a.QS;
+  const PrefillSmem L(NR_, QT, QS);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
-  uint64_t* full = bars;        // [2] Q + K part of a stage landed (TMA bytes + summary rows)
-  uint64_t* empty = bars + 2;   // [2] Q + K part consumed (QK done)
-  uint64_t* sfull = bars + 4;   // [2] per group: S ready in TMEM
-  uint64_t* pfull = bars + 6;   // [2] per group: P stored in TMEM (256 arrivals)
-  uint64_t* ofull = bars + 8;   // [2] per group: O ready in TMEM
-  uint64_t* drain = bars + 10;  // MMA drain at exit
-  uint64_t* vfull = bars + 11;  // [2] V part of a stage landed
-  uint64_t* vempty = bars + 13; // [2] V part consumed (PV done)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 16);
-  uint32_t* unit_meta = reinterpret_cast<uint32_t*>(bars + 17);  // [8] (unit << 8) | summary count
-  float* xchg = reinterpret_cast<float*>(smem + L.xchg);         // [2 groups][2 halves][256]
+  uint64_t* qfull = bars;        // [4] Q tile of unit i landed (slot i % QS)
+  uint64_t* kfull = bars + 4;    // [3] new K rows + K summary tile of unit i landed (slot i % 3)
+  uint64_t* vfull = bars + 7;    // [3] new V rows + V summary tile of unit i landed
+  uint64_t* qkdone = bars + 10;  // [4] QK(i) complete (ring i % 4)
+  uint64_t* pvdone = bars + 14;  // [4] PV(i) complete: O ready, V rows / summary tile free
+  uint64_t* sfull = bars + 18;   // [2] per group: S ready in TMEM
+  uint64_t* pfull = bars + 20;   // [2] per group: P stored in TMEM (256 arrivals)
+  uint64_t* drain = bars + 22;   // MMA drain at exit
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 23);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 24);
+  uint32_t* unit_meta = reinterpret_cast<uint32_t*>(bars + 25);  // [8] (unit << 8) | summary count
+  float* xchg = reinterpret_cast<float*>(smem + L.xchg);
 
   if (threadIdx.x == 0) {
+    for (int s = 0; s < 4; ++s) {
+      mbar_init(&qfull[s], 1);
+      mbar_init(&qkdone[s], 1);
+      mbar_init(&pvdone[s], 1);
+    }
+    for (int s = 0; s < 3; ++s) {  // TMA expect-tx arrival + producer arrival + 32 cp.async arrivals
+      mbar_init(&kfull[s], 34);
+      mbar_init(&vfull[s], 34);
+    }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&full[s], 2);
-      mbar_init(&empty[s], 1);
-      mbar_init(&vfull[s], 2);
-      mbar_init(&vempty[s], 1);
       mbar_init(&sfull[s], 1);
       mbar_init(&pfull[s], 256);
-      mbar_init(&ofull[s], 1);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -130,163 +139,189 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  constexpr int NK_ = NR_ + 16;  // keys per unit (raw slice + summary rows)
-  const int NR = NR_, QT = a.QT, G = a.G, S = a.stages;
-  const int NK = NK_;
+  constexpr int NK_ = NR_ + 16;  // keys per unit (raw window + summary rows)
+  constexpr int NR = NR_;
+  const int R = (int)L.R;
+  // this CTA's contiguous range of units
+  const int u_begin = (int)((int64_t)blockIdx.x * a.total_units / gridDim.x);
+  const int n_units = (int)((int64_t)(blockIdx.x + 1) * a.total_units / gridDim.x) - u_begin;
   auto stamp = [&](int i, int ev) {
     if (a.trace && i < 64) a.trace[((int64_t)blockIdx.x * 64 + i) * 16 + ev] = globaltimer();
   };
-  const int BS = a.route.block_size;
-  auto stage_ptr = [&](int s) { return smem + (uint32_t)s * L.stage; };
+  // ring row where unit i's key window starts (advances QT per unit, mod R)
+  auto roff = [&](int i) { return (int)(((int64_t)i * QT) % R); };
 
   if (warp == 0 || warp == kVWarp) {
     // ------------------------------------------------------------------ producers
-    // Warp 0 fills the Q + K part of each stage, warp kVWarp the V part.  Both append the
-    // unit's routed-summary rows (zero rows past the valid ones) to their K / V tile.
-    // Software-pipelined by one unit: the route and the summary-row loads of unit i+1 are
-    // issued before waiting for unit i's stage, so their latency is off the critical path.
+    // Warp 0: Q tiles (ring of QS) and the K ring; warp kVWarp: the V ring.  Per unit the
+    // producer appends the routed-summary rows to a 16-row summary tile (slot i % 3).  The
+    // route and the summary-row loads of unit i+1 are issued before waiting on unit i's
+    // buffers, so their latency is off the critical path.
     const bool isv = warp == kVWarp;
     const uint8_t* sumbase = reinterpret_cast<const uint8_t*>(isv ? a.vsum : a.ksum);
     const int64_t sb_ = isv ? a.vs_b : a.ks_b, sh_ = isv ? a.vs_h : a.ks_h, sn_ = isv ? a.vs_n : a.ks_n;
-    uint64_t* fullb = isv ? vfull : full;
-    uint64_t* emptyb = isv ? vempty : empty;
-    const uint32_t tile_off = isv ? L.v : L.k;
-    uint4 cur[8], nxt[8];
-    int ns_cur = 0, ns_nxt = 0;
-    auto fetch = [&](int u, uint4* regs) -> int {
-      const int t = u % a.ntiles, rest = u / a.ntiles, kvh = rest % a.Hkv, b = rest / a.Hkv;
-      int ids[kMaxSummaries];
-      const int ns = prefill_summaries(a.route, a.blk0 + t / a.tiles_per_block, a.window, a.route.neighbors, ids);
+    uint64_t* fullb = isv ? vfull : kfull;
+    uint64_t* doneb = isv ? pvdone : qkdone;
+    const uint32_t ring_off = isv ? L.vring : L.kring;
+    const uint32_t sum_off = isv ? L.vsum : L.ksum;
+    const CUtensorMap* tm = isv ? &tmV : &tmK;
+    // (t, kvh, b) of the current unit are advanced incrementally; the route is recomputed
+    // only when the block changes (every tiles_per_block units)
+    int ids[kMaxSummaries];
+    int ns = 0, route_blk = -1;
+    int t = 0, kvh = 0, b = 0;
+    if (n_units > 0) {
+      t = u_begin % a.ntiles;
+      const int rest = u_begin / a.ntiles;
+      kvh = rest % a.Hkv;
+      b = rest / a.Hkv;
+    }
+    for (int i = 0; i < n_units; ++i) {
+      if (i > 0 && ++t == a.ntiles) {
+        t = 0;
+        if (++kvh == a.Hkv) {
+          kvh = 0;
+          ++b;
+        }
+      }
+      const int qs = t * QT;
+      const int blk = a.blk0 + t / a.tiles_per_block;
+      if (blk != route_blk) {
+        ns = prefill_summaries(a.route, blk, a.window, a.route.neighbors, ids);
+        route_blk = blk;
+      }
+      const bool run_start = i == 0 || t == 0;
+      if (!isv) {
+        // Q tile slot i % QS is free once QK(i - QS) completed
+        const int dq = i - QS;
+        if (dq >= 0 && !mbar_wait(&qkdone[dq & 3], (uint32_t)(dq >> 2) & 1u, abort_flag, 1, a.err)) break;
+        if (lane == 0) {
+          stamp(i, 0);
+          uint8_t* qd = smem + L.q + (uint32_t)(i % QS) * 32768u;
+          uint64_t* qb = &qfull[i % QS];
+          mbar_arrive_expect_tx(qb, 32768u);
+          if (a.q_tmajor) {
+            tma_load_4d(qd, &tmQ, qb, 0, kvh * G, qs, b);
+            tma_load_4d(qd + 16384, &tmQ, qb, 64, kvh * G, qs, b);
+          } else {
+            tma_load_4d(qd, &tmQ, qb, 0, qs, kvh * G, b);
+            tma_load_4d(qd + 16384, &tmQ, qb, 64, qs, kvh * G, b);
+          }
+        }
+      }
+      // ring rows and summary tile slot i % 3 are free once the MMA reading them (QK for K,
+      // PV for V) of unit i - 3 completed; a new run rewrites a whole window: unit i - 1
+      const int dep = run_start ? i - 1 : i - 3;
+      if (dep >= 0 && !mbar_wait(&doneb[dep & 3], (uint32_t)(dep >> 2) & 1u, abort_flag, isv ? 10 : 2, a.err)) break;
+      if (lane == 0) stamp(i, isv ? 14 : 1);
+      const int k3 = i % 3;
+      if (lane == 0) {
+        const int rows = run_start ? NR : QT;
+        const int idx0 = a.kidx0 + qs + (run_start ? 0 : NR - QT);
+        const int row0 = run_start ? roff(i) : (roff(i) + NR - QT) % R;
+        mbar_arrive_expect_tx(&fullb[k3], (uint32_t)rows * 256u);
+        for (int c = 0; c < rows; c += 16) {
+          int rr = row0 + c;
+          if (rr >= R) rr -= R;
+          uint8_t* dst = smem + ring_off + (uint32_t)rr * 128u;
+          tma_load_4d(dst, tm, &fullb[k3], 0, idx0 + c, kvh, b);
+          tma_load_4d(dst + L.ring_half, tm, &fullb[k3], 64, idx0 + c, kvh, b);
+        }
+        if (!isv) stamp(i, 11);
+      }
+      // summary rows: cp.async straight into the swizzled tile, completion counted on the
+      // unit's barrier (32 lanes x .noinc); rows past the valid ones are zeroed directly
+      uint8_t* sumt = smem + sum_off + (uint32_t)k3 * 4096u;
       const uint8_t* base = sumbase + 2 * (b * sb_ + kvh * sh_);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int c = lane + 32 * j, r = c >> 4, ch = c & 15;
-        regs[j] = make_uint4(0, 0, 0, 0);
-        if (r < ns) regs[j] = ld_nc_128(base + 2 * (ids[r] * sn_) + ch * 16);
-      }
-      return ns;
-    };
-    if ((int)blockIdx.x < a.total_units) ns_cur = fetch(blockIdx.x, cur);
-    int i = 0;
-    for (int u = blockIdx.x; u < a.total_units; u += gridDim.x, ++i) {
-      const int s = i % S;
-      const uint32_t ph = (uint32_t)(i / S) & 1u;
-      const int t = u % a.ntiles, rest = u / a.ntiles, kvh = rest % a.Hkv, b = rest / a.Hkv;
-      const int qs = t * QT;
-      const int kidx = a.kidx0 + qs;
-      if (u + (int)gridDim.x < a.total_units) ns_nxt = fetch(u + gridDim.x, nxt);
-      if (i >= S && !mbar_wait(&emptyb[s], ph ^ 1u, abort_flag, isv ? 10 : 1, a.err)) break;
-      if (lane == 0) stamp(i, isv ? 14 : 0);
-      uint8_t* st = stage_ptr(s);
-      if (lane == 0) {
-        if (!isv) {
-          mbar_arrive_expect_tx(&full[s], 32768u + 2u * (uint32_t)NR * 128u);
-          if (a.q_tmajor) {
-            tma_load_4d(st + L.q, &tmQ, &full[s], 0, kvh * G, qs, b);
-            tma_load_4d(st + L.q + 16384, &tmQ, &full[s], 64, kvh * G, qs, b);
-          } else {
-            tma_load_4d(st + L.q, &tmQ, &full[s], 0, qs, kvh * G, b);
-            tma_load_4d(st + L.q + 16384, &tmQ, &full[s], 64, qs, kvh * G, b);
-          }
-          tma_load_4d(st + L.k, &tmK, &full[s], 0, kidx, kvh, b);
-          tma_load_4d(st + L.k + L.kv_half, &tmK, &full[s], 64, kidx, kvh, b);
-        } else {
-          mbar_arrive_expect_tx(&vfull[s], 2u * (uint32_t)NR * 128u);
-          tma_load_4d(st + L.v, &tmV, &vfull[s], 0, kidx, kvh, b);
-          tma_load_4d(st + L.v + L.kv_half, &tmV, &vfull[s], 64, kidx, kvh, b);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
         const int c = lane + 32 * j, r = c >> 4, ch = c & 15, half = ch >> 3, cc = ch & 7;
-        const int row = NR + r;
-        const uint32_t off = half * L.kv_half + row * 128 + ((cc ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(st + tile_off + off) = cur[j];
+        uint8_t* dst = sumt + half * 2048 + r * 128 + ((cc ^ (r & 7)) << 4);
+        if (r < ns) cp_async_16_sm(dst, base + 2 * (ids[r] * sn_) + ch * 16);
+        else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
       }
+      cp_async_mbar_arrive_noinc(&fullb[k3]);
+      if (lane == 0 && !isv) stamp(i, 12);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         stamp(i, isv ? 15 : 2);
-        if (!isv) *reinterpret_cast<volatile uint32_t*>(unit_meta + (i & 7)) = ((uint32_t)i << 8) | (uint32_t)ns_cur;
-        mbar_arrive(&fullb[s]);
+        if (!isv) *reinterpret_cast<volatile uint32_t*>(unit_meta + (i & 7)) = ((uint32_t)i << 8) | (uint32_t)ns;
+        mbar_arrive(&fullb[k3]);
       }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
-      ns_cur = ns_nxt;
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t fmt = ElemTraits<T>::kUmmaFormat;
-      const uint32_t id_qk = idesc_f16(128, NK, fmt, false);
+      const uint32_t id_qs = idesc_f16(128, 16, fmt, false);
       const uint32_t id_pv = idesc_f16(128, 128, fmt, true);
-      int n = 0;
-      for (int u = blockIdx.x; u < a.total_units; u += gridDim.x) ++n;
+      const int n = n_units;
       bool ok = true;
       auto issue_qk = [&](int i) -> bool {
-        const int s = i % S, g = i & 1;
-        // S/P tile of group g was last read by PV(i - 2): wait for it before overwriting.
-        if (i >= 2 && !mbar_wait(&ofull[g], (uint32_t)((i - 2) >> 1) & 1u, abort_flag, 7, a.err)) return false;
-        if (!mbar_wait(&full[s], (uint32_t)(i / S) & 1u, abort_flag, 2, a.err)) return false;
-        stamp(i, 3);
+        const int g = i & 1, k3 = i % 3;
         tc_fence_after();
-        const uint32_t base = smem_u32(stage_ptr(s));
+        fence_proxy_async_smem();  // summary rows arrived through cp.async (generic proxy)
+        stamp(i, 3);
+        const uint32_t qb = smem_u32(smem + L.q + (uint32_t)(i % QS) * 32768u);
+        const uint32_t kb = smem_u32(smem + L.kring);
+        const uint32_t sb = smem_u32(smem + L.ksum + (uint32_t)k3 * 4096u);
         const uint32_t dS = tmem + (uint32_t)g * 128u;
+        const int r0 = roff(i);
+        const int n1 = (R - r0) < NR ? (R - r0) : NR;
+        const int n2 = NR - n1;
+        const uint32_t id1 = idesc_f16(128, n1, fmt, false);
+        const uint32_t id2 = idesc_f16(128, n2 > 0 ? n2 : 16, fmt, false);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t kin = (uint32_t)(kk & 3) * 32u;
-          const uint64_t aq = desc_sw128(base + L.q + (kk >> 2) * 16384u + kin, 16, 1024);
-          const uint64_t bk = desc_sw128(base + L.k + (kk >> 2) * L.kv_half + kin, 16, 1024);
-          mma_f16_ss(dS, aq, bk, id_qk, kk > 0);
+          const uint32_t hoff = (uint32_t)(kk >> 2) * L.ring_half;
+          const uint64_t aq = desc_sw128(qb + (kk >> 2) * 16384u + kin, 16, 1024);
+          mma_f16_ss(dS, aq, desc_sw128(kb + hoff + (uint32_t)r0 * 128u + kin, 16, 1024), id1, kk > 0);
+          if (n2 > 0) mma_f16_ss(dS + (uint32_t)n1, aq, desc_sw128(kb + hoff + kin, 16, 1024), id2, kk > 0);
+          mma_f16_ss(dS + (uint32_t)NR, aq, desc_sw128(sb + (kk >> 2) * 2048u + kin, 16, 1024), id_qs, kk > 0);
         }
         mma_commit(&sfull[g]);
-        mma_commit(&empty[s]);
+        mma_commit(&qkdone[i & 3]);
         return true;
       };
       auto issue_pv = [&](int i) -> bool {
-        const int s = i % S, g = i & 1;
-        if (!mbar_wait(&pfull[g], (uint32_t)(i >> 1) & 1u, abort_flag, 3, a.err)) return false;
-        if (!mbar_wait(&vfull[s], (uint32_t)(i / S) & 1u, abort_flag, 9, a.err)) return false;
-        stamp(i, 4);
+        const int g = i & 1, k3 = i % 3;
         tc_fence_after();
-        const uint32_t base = smem_u32(stage_ptr(s));
+        fence_proxy_async_smem();
+        stamp(i, 4);
+        const uint32_t vb = smem_u32(smem + L.vring);
+        const uint32_t vs = smem_u32(smem + L.vsum + (uint32_t)k3 * 4096u);
         const uint32_t aP = tmem + (uint32_t)g * 128u;
         const uint32_t dO = tmem + 256u + (uint32_t)g * 128u;
-        for (int ks = 0; ks < NK / 16; ++ks) {
-          const uint64_t bv = desc_sw128(base + L.v + (uint32_t)ks * 2048u, L.kv_half, 1024);
-          mma_f16_ts(dO, aP + (uint32_t)ks * 8u, bv, id_pv, ks > 0);
+        const int r0 = roff(i);
+#pragma unroll 1
+        for (int ks = 0; ks < NR / 16; ++ks) {
+          int row = r0 + ks * 16;
+          if (row >= R) row -= R;
+          mma_f16_ts(dO, aP + (uint32_t)ks * 8u, desc_sw128(vb + (uint32_t)row * 128u, L.ring_half, 1024), id_pv,
+                     ks > 0);
         }
-        mma_commit(&ofull[g]);
-        mma_commit(&vempty[s]);
+        mma_f16_ts(dO, aP + (uint32_t)(NR / 16) * 8u, desc_sw128(vs, 2048, 1024), id_pv, 1);
+        mma_commit(&pvdone[i & 3]);
         return true;
       };
-      // Issue whichever is ready: PV(j) once group j&1 stored P(j); QK(j) once unit j's
-      // stage landed and PV(j-2) (same S/P tile) completed.  PV is preferred.  With one
-      // stage, QK(j) also needs PV(j-1) issued (the stage is shared).
-      int next_qk = 0, next_pv = 0, seen_full = 0, seen_v = 0;
+      // Issue whichever is ready (PV preferred): PV(j) once group j%2 stored P(j) and V(j)
+      // landed; QK(j) once Q(j) and K(j) landed and PV(j-2) (same S/P tile) completed.
+      int next_qk = 0, next_pv = 0;
       int64_t last = clock64();
       uint32_t spins = 0;
       while (next_pv < n && ok) {
         bool progressed = false;
         if (next_pv < next_qk && mbar_test_wait(&pfull[next_pv & 1], (uint32_t)(next_pv >> 1) & 1u) &&
-            mbar_test_wait(&vfull[next_pv % S], (uint32_t)(next_pv / S) & 1u)) {
+            mbar_test_wait(&vfull[next_pv % 3], (uint32_t)(next_pv / 3) & 1u)) {
           ok = issue_pv(next_pv++);
           progressed = true;
-        }
-        if (!progressed && next_pv < n && seen_v < next_pv + 1 &&
-            mbar_test_wait(&vfull[next_pv % S], (uint32_t)(next_pv / S) & 1u)) {
-          stamp(next_pv, 1);
-          seen_v = next_pv + 1;
-        }
-        if (!progressed && next_qk < n && seen_full < next_qk + 1 &&
-            mbar_test_wait(&full[next_qk % S], (uint32_t)(next_qk / S) & 1u)) {
-          stamp(next_qk, 12);
-          seen_full = next_qk + 1;
-        }
-        if (progressed) {
         } else if (next_qk < n && next_qk < next_pv + 2 &&
-                   (next_qk < 2 || mbar_test_wait(&ofull[next_qk & 1], (uint32_t)((next_qk - 2) >> 1) & 1u)) &&
-                   mbar_test_wait(&full[next_qk % S], (uint32_t)(next_qk / S) & 1u)) {
+                   (next_qk < 2 ||
+                    mbar_test_wait(&pvdone[(next_qk - 2) & 3], (uint32_t)((next_qk - 2) >> 2) & 1u)) &&
+                   mbar_test_wait(&qfull[next_qk % QS], (uint32_t)(next_qk / QS) & 1u) &&
+                   mbar_test_wait(&kfull[next_qk % 3], (uint32_t)(next_qk / 3) & 1u)) {
           ok = issue_qk(next_qk++);
           progressed = true;
         }
@@ -328,9 +363,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* xo = xchg + (grp * 2 + (half ^ 1)) * 256;  // partner's
     const uint32_t bar_id = 1u + (uint32_t)(grp * 4 + quad);
     const float sl2 = a.scale_log2;
-    int i = 0;
-    for (int u = blockIdx.x; u < a.total_units; u += gridDim.x, ++i) {
-      if ((i & 1) != grp) continue;
+    for (int i = grp; i < n_units; i += 2) {
+      const int u = u_begin + i;
       const uint32_t par = (uint32_t)(i >> 1) & 1u;
       const int t = u % a.ntiles, rest = u / a.ntiles, kvh = rest % a.Hkv, b = rest / a.Hkv;
       const int qs = t * QT;
@@ -384,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_bar_sync(bar_id, 64);
       m = fmaxf(m, xo[row]);
       const float mb = m > -INFINITY ? m * sl2 : 0.f;
-      if (row == 0 && half == 0) stamp(i, 10);
+
       float lp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int k0 = 0; k0 < kMaxCols; k0 += 16) {
@@ -410,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_bar_sync(bar_id, 64);
       l += xo[128 + row];
 
-      if (!mbar_wait(&ofull[grp], par, abort_flag, 5, a.err)) break;
+      if (!mbar_wait(&pvdone[i & 3], (uint32_t)(i >> 2) & 1u, abort_flag, 5, a.err)) break;
       if (row == 0 && half == 0) stamp(i, 7);
       tc_fence_after();
       const float inv = (valid_row && l > 0.f) ? 1.f / l : 0.f;
@@ -451,6 +485,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ----------------------------------------------------------------------------- host
 int* device_error_word();  // kernels.cu
+namespace staged {
+int launch_prefill_staged(const bna_tensor4*, const bna_tensor4*, const bna_tensor4*, const bna_tensor4*,
+                          const bna_tensor4*, bna_tensor4*, float*, int64_t, int64_t, int, const bna_route*, int, int64_t,
+                          int64_t, int64_t, float, cudaStream_t);
+}
 
 // Optional prefill timeline buffer (device, >= grid * 64 * 16 uint64), set by
 // bna_set_prefill_trace; nullptr disables the stamps.
@@ -544,10 +583,12 @@ int launch_prefill(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  a.stages = 2;
-  if ((int)PrefillSmem(a.NR, 2).total > max_smem) a.stages = 1;
-  const uint32_t smem = PrefillSmem(a.NR, a.stages).total;
-  if ((int)smem > max_smem) return fail(BNA_UNSUPPORTED, "prefill tile does not fit in shared memory");
+  a.QS = 3;
+  if ((int)PrefillSmem(a.NR, a.QT, 3).total > max_smem) a.QS = 2;
+  const uint32_t smem = PrefillSmem(a.NR, a.QT, a.QS).total;
+  if ((int)smem > max_smem)  // rings too large for this shape: stage-based variant
+    return staged::launch_prefill_staged(q, k, v, ks, vs, out, lse, ls_b, ls_h, dtype, route, window, q_pos0, kv_pos0,
+                                         total_len, scale, stream);
 
   const CUtensorMapDataType dt = dtype == BNA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap mq, mk, mv;
@@ -565,7 +606,7 @@ int launch_prefill(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4
   }
   if (rc) return rc;
   const int okv[3] = {2, 1, 0};
-  const uint32_t bkv[3] = {(uint32_t)a.NR, 1, 1};
+  const uint32_t bkv[3] = {16, 1, 1};  // ring loads in 16-row boxes
   if ((rc = encode_map(&mk, k, dt, okv, bkv, "k"))) return rc;
   if ((rc = encode_map(&mv, v, dt, okv, bkv, "v"))) return rc;
 

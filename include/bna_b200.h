@@ -130,6 +130,12 @@ BNA_API int bna_compress_blocks(const bna_tensor4* x, bna_tensor4* out, int32_t 
                         int64_t pos0, int32_t n_blocks, int64_t valid_len, int64_t ring,
                         int64_t slot0, void* stream);
 
+/* The same for a K/V pair in one launch (shapes of k and v, and of k_out and v_out, equal). */
+BNA_API int bna_compress_kv_blocks(const bna_tensor4* k, const bna_tensor4* v, bna_tensor4* k_out,
+                                   bna_tensor4* v_out, int32_t dtype, int32_t block_size, int64_t pos0,
+                                   int32_t n_blocks, int64_t valid_len, int64_t ring, int64_t slot0,
+                                   void* stream);
+
 /* ---- K2: prefill attention on tcgen05/TMEM (:1046-1122) -------------------------------
  * q [B,Hq,Tq,dh] (any strides, dh contiguous, 16-byte aligned rows), k/v [B,Hkv,Tk,dh],
  * k_sum/v_sum [B,Hkv,N,dh] block means, out [B,Hq,Tq,dh] (same dtype), lse (optional,
