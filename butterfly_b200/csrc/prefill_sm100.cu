@@ -252,7 +252,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the scheduler (converged, warp-uniform values); barrier polls are
+    // broadcast from lane 0 and one elected lane issues the MMAs.
+    {
       constexpr uint32_t fmt = ElemTraits<T>::kUmmaFormat;
       const uint32_t id_qs = idesc_f16(128, 16, fmt, false);
       const uint32_t id_pv = idesc_f16(128, 128, fmt, true);
@@ -262,7 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int g = i & 1, k3 = i % 3;
         tc_fence_after();
         fence_proxy_async_smem();  // summary rows arrived through cp.async (generic proxy)
-        stamp(i, 3);
+        if (lane == 0) stamp(i, 3);
         const uint32_t qb = smem_u32(smem + L.q + (uint32_t)(i % QS) * 32768u);
         const uint32_t kb = smem_u32(smem + L.kring);
         const uint32_t sb = smem_u32(smem + L.ksum + (uint32_t)k3 * 4096u);
@@ -272,56 +274,67 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int n2 = NR - n1;
         const uint32_t id1 = idesc_f16(128, n1, fmt, false);
         const uint32_t id2 = idesc_f16(128, n2 > 0 ? n2 : 16, fmt, false);
+        // descriptors built once; k-step kk adds (kk & 3) * 32 B inside the swizzle atom and the
+        // half offset for kk >= 4 (descriptor start addresses count 16-byte units)
+        const uint64_t dq0 = desc_sw128(qb, 16, 1024);
+        const uint64_t dk1 = desc_sw128(kb + (uint32_t)r0 * 128u, 16, 1024);
+        const uint64_t dk2 = desc_sw128(kb, 16, 1024);
+        const uint64_t ds0 = desc_sw128(sb, 16, 1024);
+        const uint64_t rh = L.ring_half >> 4;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t kin = (uint32_t)(kk & 3) * 32u;
-          const uint32_t hoff = (uint32_t)(kk >> 2) * L.ring_half;
-          const uint64_t aq = desc_sw128(qb + (kk >> 2) * 16384u + kin, 16, 1024);
-          mma_f16_ss(dS, aq, desc_sw128(kb + hoff + (uint32_t)r0 * 128u + kin, 16, 1024), id1, kk > 0);
-          if (n2 > 0) mma_f16_ss(dS + (uint32_t)n1, aq, desc_sw128(kb + hoff + kin, 16, 1024), id2, kk > 0);
-          mma_f16_ss(dS + (uint32_t)NR, aq, desc_sw128(sb + (kk >> 2) * 2048u + kin, 16, 1024), id_qs, kk > 0);
+          const uint64_t kin = (uint64_t)((kk & 3) * 2);
+          const uint64_t aq = dq0 + kin + (kk >= 4 ? 1024u : 0u);
+          const uint64_t hk = kk >= 4 ? rh : 0;
+          mma_f16_ss_warp(dS, aq, dk1 + kin + hk, id1, kk > 0);
+          if (n2 > 0) mma_f16_ss_warp(dS + (uint32_t)n1, aq, dk2 + kin + hk, id2, kk > 0);
+          mma_f16_ss_warp(dS + (uint32_t)NR, aq, ds0 + kin + (kk >= 4 ? 128u : 0u), id_qs, kk > 0);
         }
-        mma_commit(&sfull[g]);
-        mma_commit(&qkdone[i & 3]);
+        mma_commit_warp(&sfull[g]);
+        mma_commit_warp(&qkdone[i & 3]);
         return true;
       };
       auto issue_pv = [&](int i) -> bool {
         const int g = i & 1, k3 = i % 3;
         tc_fence_after();
         fence_proxy_async_smem();
-        stamp(i, 4);
+        if (lane == 0) stamp(i, 4);
         const uint32_t vb = smem_u32(smem + L.vring);
         const uint32_t vs = smem_u32(smem + L.vsum + (uint32_t)k3 * 4096u);
         const uint32_t aP = tmem + (uint32_t)g * 128u;
         const uint32_t dO = tmem + 256u + (uint32_t)g * 128u;
         const int r0 = roff(i);
-#pragma unroll 1
+        const uint64_t dv0 = desc_sw128(vb, L.ring_half, 1024);  // + row * 128 B per key step
+#pragma unroll
         for (int ks = 0; ks < NR / 16; ++ks) {
           int row = r0 + ks * 16;
           if (row >= R) row -= R;
-          mma_f16_ts(dO, aP + (uint32_t)ks * 8u, desc_sw128(vb + (uint32_t)row * 128u, L.ring_half, 1024), id_pv,
-                     ks > 0);
+          mma_f16_ts_warp(dO, aP + (uint32_t)ks * 8u, dv0 + (uint64_t)(row * 8), id_pv, ks > 0);
         }
-        mma_f16_ts(dO, aP + (uint32_t)(NR / 16) * 8u, desc_sw128(vs, 2048, 1024), id_pv, 1);
-        mma_commit(&pvdone[i & 3]);
+        mma_f16_ts_warp(dO, aP + (uint32_t)(NR / 16) * 8u, desc_sw128(vs, 2048, 1024), id_pv, 1);
+        mma_commit_warp(&pvdone[i & 3]);
         return true;
       };
       // Issue whichever is ready (PV preferred): PV(j) once group j%2 stored P(j) and V(j)
       // landed; QK(j) once Q(j) and K(j) landed and PV(j-2) (same S/P tile) completed.
+      auto ready = [&](uint64_t* bar, uint32_t parity) -> bool {
+        const bool r = lane == 0 ? mbar_test_wait(bar, parity) : false;
+        return __shfl_sync(0xffffffffu, r ? 1 : 0, 0) != 0;
+      };
       int next_qk = 0, next_pv = 0;
       int64_t last = clock64();
       uint32_t spins = 0;
       while (next_pv < n && ok) {
         bool progressed = false;
-        if (next_pv < next_qk && mbar_test_wait(&pfull[next_pv & 1], (uint32_t)(next_pv >> 1) & 1u) &&
-            mbar_test_wait(&vfull[next_pv % 3], (uint32_t)(next_pv / 3) & 1u)) {
+        if (next_pv < next_qk && ready(&pfull[next_pv & 1], (uint32_t)(next_pv >> 1) & 1u) &&
+            ready(&vfull[next_pv % 3], (uint32_t)(next_pv / 3) & 1u)) {
           ok = issue_pv(next_pv++);
           progressed = true;
         } else if (next_qk < n && next_qk < next_pv + 2 &&
                    (next_qk < 2 ||
-                    mbar_test_wait(&pvdone[(next_qk - 2) & 3], (uint32_t)((next_qk - 2) >> 2) & 1u)) &&
-                   mbar_test_wait(&qfull[next_qk % QS], (uint32_t)(next_qk / QS) & 1u) &&
-                   mbar_test_wait(&kfull[next_qk % 3], (uint32_t)(next_qk / 3) & 1u)) {
+                    ready(&pvdone[(next_qk - 2) & 3], (uint32_t)((next_qk - 2) >> 2) & 1u)) &&
+                   ready(&qfull[next_qk % QS], (uint32_t)(next_qk / QS) & 1u) &&
+                   ready(&kfull[next_qk % 3], (uint32_t)(next_qk / 3) & 1u)) {
           ok = issue_qk(next_qk++);
           progressed = true;
         }
@@ -329,17 +342,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           spins = 0;
           last = clock64();
         } else if ((++spins & 255) == 0) {
-          if (*abort_flag) break;
-          if (clock64() - last > kWaitTimeoutCycles) {
-            *abort_flag = 1;
-            if (a.err) atomicCAS(a.err, 0, 0x1000 | 8);
+          if (__shfl_sync(0xffffffffu, *abort_flag, 0)) break;
+          if (__shfl_sync(0xffffffffu, (clock64() - last > kWaitTimeoutCycles) ? 1 : 0, 0)) {
+            if (lane == 0) {
+              *abort_flag = 1;
+              if (a.err) atomicCAS(a.err, 0, 0x1000 | 8);
+            }
             break;
           }
         }
       }
       volatile int never_abort = 0;
-      mma_commit(drain);
-      mbar_wait(drain, 0, &never_abort, 6, a.err);
+      mma_commit_warp(drain);
+      if (lane == 0) mbar_wait(drain, 0, &never_abort, 6, a.err);
     }
     __syncwarp();
   } else {
