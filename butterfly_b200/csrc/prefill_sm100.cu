@@ -233,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // unit's barrier (32 lanes x .noinc); rows past the valid ones are zeroed directly
       uint8_t* sumt = smem + sum_off + (uint32_t)k3 * 4096u;
       const uint8_t* base = sumbase + 2 * (b * sb_ + kvh * sh_);
-#pragma unroll
+#pragma unroll 1
       for (int j = 0; j < 8; ++j) {
         const int c = lane + 32 * j, r = c >> 4, ch = c & 15, half = ch >> 3, cc = ch & 7;
         uint8_t* dst = sumt + half * 2048 + r * 128 + ((cc ^ (r & 7)) << 4);
@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t dk2 = desc_sw128(kb, 16, 1024);
         const uint64_t ds0 = desc_sw128(sb, 16, 1024);
         const uint64_t rh = L.ring_half >> 4;
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t kin = (uint64_t)((kk & 3) * 2);
           const uint64_t aq = dq0 + kin + (kk >= 4 ? 1024u : 0u);
@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t dO = tmem + 256u + (uint32_t)g * 128u;
         const int r0 = roff(i);
         const uint64_t dv0 = desc_sw128(vb, L.ring_half, 1024);  // + row * 128 B per key step
-#pragma unroll
+#pragma unroll 1
         for (int ks = 0; ks < NR / 16; ++ks) {
           int row = r0 + ks * 16;
           if (row >= R) row -= R;
