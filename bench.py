@@ -368,8 +368,8 @@ def prefill_trace(dev):
     _lib.lib().bna_set_prefill_trace(None)
     tr = buf.view(nsm, 64, 16).cpu().numpy().astype("int64")
     t0 = tr[:, :, :16][tr[:, :, :16] > 0].min()
-    names = ["q_issued", "k_dep_ok", "prod_full", "mma_qk", "mma_pv", "smx_s", "smx_p", "smx_o", "smx_done",
-             "route_begin", "route_end", "k_tma_issued", "cpasync_issued", "smx_meta", "v_start", "v_full"]
+    names = ["q_issued", "k_issued", "prod_full", "mma_qk", "mma_pv", "smx_s", "smx_p", "smx_o", "smx_done",
+             "-", "-", "-", "-", "-", "-", "v_full"]
     for cta in (0,):
         print(f"cta {cta} (us from kernel start)")
         for i in range(16):

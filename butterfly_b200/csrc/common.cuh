@@ -68,6 +68,13 @@ __device__ __forceinline__ void st_128(void* p, uint4 v) {
   asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
 }
+// 256-bit global store (sm_100): one 32-byte chunk per lane halves the cache-line
+// requests of row-per-lane stores compared with 16-byte stores.
+__device__ __forceinline__ void st_256(void* p, const uint32_t* v) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+               "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
 
 // Host-side error reporting (thread-local last error string).
 void set_error(const std::string& msg);

@@ -28,6 +28,7 @@
 //   warps 2..17   two softmax/epilogue groups of 8 warps (units alternate between them);
 //                 two warps share each TMEM lane quarter and split the columns
 // TMEM (512 columns): group g's S/P tile at [128g, 128g+128), its O tile at 256 + 128g.
+#include <type_traits>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -52,6 +53,7 @@ struct PrefillArgs {
   int64_t ks_b, ks_h, ks_n, vs_b, vs_h, vs_n;
   void* out;
   int64_t os_b, os_h, os_t;
+  int o_st256;  // output base and strides are 32-byte multiples: 256-bit stores
   float* lse;
   int64_t ls_b, ls_h;
   int* err;         // device error word
@@ -59,16 +61,23 @@ struct PrefillArgs {
 };
 
 // Shared-memory plan (1024-byte aligned regions).
+//   q      QS tiles x 2 halves x 128 rows x 128 B
+//   kslot  kKSlots slots; a slot holds a tile's NR window rows followed by its 16 summary
+//          rows, so one MMA of N = NR + 16 covers both (2 halves x (NR + 16) rows x 128 B)
+//   vring  V window rows as a ring of R = NR + 2 QT rows (2 halves)
+//   vsum   3 slots x 2 halves x 16 V summary rows x 128 B
+constexpr int kKSlots = 2;
 struct PrefillSmem {
-  uint32_t R, q, kring, ring_half, vring, ksum, vsum, xchg, bars, total;
+  uint32_t R, q, kslot, kslot_half, kslot_size, ring_half, vring, vsum, xchg, bars, total;
   __host__ __device__ PrefillSmem(int NR, int QT, int QS) {
-    R = (uint32_t)(NR + 2 * QT);        // ring rows (multiple of 16)
-    q = 0;                              // QS tiles x 2 halves x 128 rows x 128 B
-    ring_half = R * 128;                // one 64-column half of a ring
-    kring = (uint32_t)QS * 32768;
-    vring = kring + 2 * ring_half;
-    ksum = vring + 2 * ring_half;       // 3 slots x 2 halves x 16 rows x 128 B
-    vsum = ksum + 3 * 4096;
+    R = (uint32_t)(NR + 2 * QT);        // V ring rows (multiple of 16)
+    q = 0;
+    kslot = (uint32_t)QS * 32768;
+    kslot_half = (uint32_t)(NR + 16) * 128;  // multiple of 1024 (NR is a multiple of 16)
+    kslot_size = 2 * kslot_half;
+    ring_half = R * 128;                // one 64-column half of the V ring
+    vring = kslot + kKSlots * kslot_size;
+    vsum = vring + 2 * ring_half;
     xchg = vsum + 3 * 4096;             // [2 groups][2 buffers][2 halves][128] row maxima
     bars = xchg + 4096;
     total = bars + 512 + 1024;          // + alignment slack
@@ -80,6 +89,12 @@ namespace {
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kThreads = 608;  // 19 warps
 constexpr int kVWarp = 18;     // V producer
+
+// Route of a query block, out of line: producers call it once per block (every few tiles),
+// and one shared copy keeps the hot loops small in the instruction cache.
+__device__ __noinline__ int prefill_summaries_ool(const bna_route& r, int blk, int window, int* ids) {
+  return prefill_summaries(r, blk, window, r.neighbors, ids);
+}
 
 template <typename T, int NR_>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -94,7 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* qfull = bars;        // [4] Q tile of unit i landed (slot i % QS)
-  uint64_t* kfull = bars + 4;    // [3] new K rows + K summary tile of unit i landed (slot i % 3)
+  uint64_t* kfull = bars + 4;    // [kKSlots] K window + summary rows of unit i landed (slot i % kKSlots)
   uint64_t* vfull = bars + 7;    // [3] new V rows + V summary tile of unit i landed
   uint64_t* qkdone = bars + 10;  // [4] QK(i) complete (ring i % 4)
   uint64_t* pvdone = bars + 14;  // [4] PV(i) complete: O ready, V rows / summary tile free
@@ -112,10 +127,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&qkdone[s], 1);
       mbar_init(&pvdone[s], 1);
     }
-    for (int s = 0; s < 3; ++s) {  // TMA expect-tx arrival + producer arrival + 32 cp.async arrivals
-      mbar_init(&kfull[s], 34);
-      mbar_init(&vfull[s], 34);
-    }
+    // TMA expect-tx arrival + producer arrival + 32 cp.async arrivals
+    for (int s = 0; s < kKSlots; ++s) mbar_init(&kfull[s], 34);
+    for (int s = 0; s < 3; ++s) mbar_init(&vfull[s], 34);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sfull[s], 1);
       mbar_init(&pfull[s], 256);
@@ -153,18 +167,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0 || warp == kVWarp) {
     // ------------------------------------------------------------------ producers
-    // Warp 0: Q tiles (ring of QS) and the K ring; warp kVWarp: the V ring.  Per unit the
-    // producer appends the routed-summary rows to a 16-row summary tile (slot i % 3).  The
-    // route and the summary-row loads of unit i+1 are issued before waiting on unit i's
-    // buffers, so their latency is off the critical path.
+    // Warp 0: Q tiles (ring of QS) and K slots (kKSlots); warp kVWarp: the V ring.  Per unit
+    // the producer also gathers the routed-summary rows: behind the window rows of the K
+    // slot, and into a 16-row V summary tile (slot i % 3).
     const bool isv = warp == kVWarp;
     const uint8_t* sumbase = reinterpret_cast<const uint8_t*>(isv ? a.vsum : a.ksum);
     const int64_t sb_ = isv ? a.vs_b : a.ks_b, sh_ = isv ? a.vs_h : a.ks_h, sn_ = isv ? a.vs_n : a.ks_n;
-    uint64_t* fullb = isv ? vfull : kfull;
-    uint64_t* doneb = isv ? pvdone : qkdone;
-    const uint32_t ring_off = isv ? L.vring : L.kring;
-    const uint32_t sum_off = isv ? L.vsum : L.ksum;
-    const CUtensorMap* tm = isv ? &tmV : &tmK;
     // (t, kvh, b) of the current unit are advanced incrementally; the route is recomputed
     // only when the block changes (every tiles_per_block units)
     int ids[kMaxSummaries];
@@ -190,11 +198,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         ns = prefill_summaries(a.route, blk, a.window, a.route.neighbors, ids);
         route_blk = blk;
       }
-      const bool run_start = i == 0 || t == 0;
+      uint64_t* fb;
+      uint8_t* sumt;     // summary rows: row r of half h at sumt + h * sum_half + r * 128
+      uint32_t sum_half;
       if (!isv) {
-        // Q tile slot i % QS is free once QK(i - QS) completed
-        const int dq = i - QS;
+        // Q slot i % QS is free once QK(i - QS) completed and K slot i % kKSlots once
+        // QK(i - kKSlots) did; a commit covers every earlier MMA, so one wait does both
+        const int dq = i - (QS < kKSlots ? QS : kKSlots);
         if (dq >= 0 && !mbar_wait(&qkdone[dq & 3], (uint32_t)(dq >> 2) & 1u, abort_flag, 1, a.err)) break;
+        uint8_t* kd = smem + L.kslot + (uint32_t)(i % kKSlots) * L.kslot_size;
+        fb = &kfull[i % kKSlots];
         if (lane == 0) {
           stamp(i, 0);
           uint8_t* qd = smem + L.q + (uint32_t)(i % QS) * 32768u;
@@ -207,105 +220,101 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_4d(qd, &tmQ, qb, 0, qs, kvh * G, b);
             tma_load_4d(qd + 16384, &tmQ, qb, 64, qs, kvh * G, b);
           }
+          // the whole window (keys before position 0 read as zeros and are masked)
+          mbar_arrive_expect_tx(fb, (uint32_t)NR * 256u);
+          tma_load_4d(kd, &tmK, fb, 0, a.kidx0 + qs, kvh, b);
+          tma_load_4d(kd + L.kslot_half, &tmK, fb, 64, a.kidx0 + qs, kvh, b);
+          stamp(i, 1);
         }
-      }
-      // ring rows and summary tile slot i % 3 are free once the MMA reading them (QK for K,
-      // PV for V) of unit i - 3 completed; a new run rewrites a whole window: unit i - 1
-      const int dep = run_start ? i - 1 : i - 3;
-      if (dep >= 0 && !mbar_wait(&doneb[dep & 3], (uint32_t)(dep >> 2) & 1u, abort_flag, isv ? 10 : 2, a.err)) break;
-      if (lane == 0) stamp(i, isv ? 14 : 1);
-      const int k3 = i % 3;
-      if (lane == 0) {
-        const int rows = run_start ? NR : QT;
-        const int idx0 = a.kidx0 + qs + (run_start ? 0 : NR - QT);
-        const int row0 = run_start ? roff(i) : (roff(i) + NR - QT) % R;
-        mbar_arrive_expect_tx(&fullb[k3], (uint32_t)rows * 256u);
-        for (int c = 0; c < rows; c += 16) {
-          int rr = row0 + c;
-          if (rr >= R) rr -= R;
-          uint8_t* dst = smem + ring_off + (uint32_t)rr * 128u;
-          tma_load_4d(dst, tm, &fullb[k3], 0, idx0 + c, kvh, b);
-          tma_load_4d(dst + L.ring_half, tm, &fullb[k3], 64, idx0 + c, kvh, b);
+        sumt = kd + (uint32_t)NR * 128u;
+        sum_half = L.kslot_half;
+      } else {
+        // V ring rows and summary tile i % 3 are free once PV(i - 3) completed; a new run
+        // rewrites a whole window: PV(i - 1)
+        const bool run_start = i == 0 || t == 0;
+        const int dep = run_start ? i - 1 : i - 3;
+        if (dep >= 0 && !mbar_wait(&pvdone[dep & 3], (uint32_t)(dep >> 2) & 1u, abort_flag, 10, a.err)) break;
+        fb = &vfull[i % 3];
+        if (lane == 0) {
+          const int rows = run_start ? NR : QT;
+          const int idx0 = a.kidx0 + qs + (run_start ? 0 : NR - QT);
+          const int row0 = run_start ? roff(i) : (roff(i) + NR - QT) % R;
+          mbar_arrive_expect_tx(fb, (uint32_t)rows * 256u);
+          for (int c = 0; c < rows; c += 16) {
+            int rr = row0 + c;
+            if (rr >= R) rr -= R;
+            uint8_t* dst = smem + L.vring + (uint32_t)rr * 128u;
+            tma_load_4d(dst, &tmV, fb, 0, idx0 + c, kvh, b);
+            tma_load_4d(dst + L.ring_half, &tmV, fb, 64, idx0 + c, kvh, b);
+          }
         }
-        if (!isv) stamp(i, 11);
+        sumt = smem + L.vsum + (uint32_t)(i % 3) * 4096u;
+        sum_half = 2048;
       }
-      // summary rows: cp.async straight into the swizzled tile, completion counted on the
-      // unit's barrier (32 lanes x .noinc); rows past the valid ones are zeroed directly
-      uint8_t* sumt = smem + sum_off + (uint32_t)k3 * 4096u;
+      // summary rows: cp.async straight into the swizzled rows, completion counted on the
+      // unit's barrier (32 lanes x .noinc); rows past the valid ones are zeroed directly.
+      // Summary rows start on an 8-row boundary, so the swizzle phase is r & 7.
       const uint8_t* base = sumbase + 2 * (b * sb_ + kvh * sh_);
 #pragma unroll 1
       for (int j = 0; j < 8; ++j) {
         const int c = lane + 32 * j, r = c >> 4, ch = c & 15, half = ch >> 3, cc = ch & 7;
-        uint8_t* dst = sumt + half * 2048 + r * 128 + ((cc ^ (r & 7)) << 4);
+        uint8_t* dst = sumt + half * sum_half + r * 128 + ((cc ^ (r & 7)) << 4);
         if (r < ns) cp_async_16_sm(dst, base + 2 * (ids[r] * sn_) + ch * 16);
         else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
       }
-      cp_async_mbar_arrive_noinc(&fullb[k3]);
-      if (lane == 0 && !isv) stamp(i, 12);
+      cp_async_mbar_arrive_noinc(fb);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         stamp(i, isv ? 15 : 2);
         if (!isv) *reinterpret_cast<volatile uint32_t*>(unit_meta + (i & 7)) = ((uint32_t)i << 8) | (uint32_t)ns;
-        mbar_arrive(&fullb[k3]);
+        mbar_arrive(fb);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    // The whole warp runs the scheduler (converged, warp-uniform values); barrier polls are
-    // broadcast from lane 0 and one elected lane issues the MMAs.
+    // The whole warp issues (converged, warp-uniform operands; one elected lane per MMA) in a
+    // fixed order QK(0), QK(1), PV(0), QK(2), PV(1), ...  Waits are taken by every lane and
+    // combined with a vote, so the branches stay warp-uniform.
     {
       constexpr uint32_t fmt = ElemTraits<T>::kUmmaFormat;
-      const uint32_t id_qs = idesc_f16(128, 16, fmt, false);
+      const uint32_t id_qk = idesc_f16(128, NK_, fmt, false);
       const uint32_t id_pv = idesc_f16(128, 128, fmt, true);
       const int n = n_units;
-      bool ok = true;
-      auto issue_qk = [&](int i) -> bool {
-        const int g = i & 1, k3 = i % 3;
+      auto wait_all = [&](uint64_t* bar, uint32_t parity, int site) -> bool {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, site, a.err)) != 0;
+      };
+      auto issue_qk = [&](int i) {
+        const int g = i & 1;
         tc_fence_after();
         fence_proxy_async_smem();  // summary rows arrived through cp.async (generic proxy)
         if (lane == 0) stamp(i, 3);
-        const uint32_t qb = smem_u32(smem + L.q + (uint32_t)(i % QS) * 32768u);
-        const uint32_t kb = smem_u32(smem + L.kring);
-        const uint32_t sb = smem_u32(smem + L.ksum + (uint32_t)k3 * 4096u);
+        // S[128 x NK] = Q[128 x 128] . [window rows | summary rows]^T: one MMA per 16-wide
+        // k-step; k-step kk adds (kk & 3) * 32 B inside the swizzle atom and the half offset
+        // for kk >= 4 (descriptor start addresses count 16-byte units)
+        const uint64_t dq0 = desc_sw128(smem_u32(smem + L.q + (uint32_t)(i % QS) * 32768u), 16, 1024);
+        const uint64_t dk0 = desc_sw128(smem_u32(smem + L.kslot + (uint32_t)(i % kKSlots) * L.kslot_size), 16, 1024);
+        const uint64_t kh = L.kslot_half >> 4;
         const uint32_t dS = tmem + (uint32_t)g * 128u;
-        const int r0 = roff(i);
-        const int n1 = (R - r0) < NR ? (R - r0) : NR;
-        const int n2 = NR - n1;
-        const uint32_t id1 = idesc_f16(128, n1, fmt, false);
-        const uint32_t id2 = idesc_f16(128, n2 > 0 ? n2 : 16, fmt, false);
-        // descriptors built once; k-step kk adds (kk & 3) * 32 B inside the swizzle atom and the
-        // half offset for kk >= 4 (descriptor start addresses count 16-byte units)
-        const uint64_t dq0 = desc_sw128(qb, 16, 1024);
-        const uint64_t dk1 = desc_sw128(kb + (uint32_t)r0 * 128u, 16, 1024);
-        const uint64_t dk2 = desc_sw128(kb, 16, 1024);
-        const uint64_t ds0 = desc_sw128(sb, 16, 1024);
-        const uint64_t rh = L.ring_half >> 4;
-#pragma unroll 1
+#pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t kin = (uint64_t)((kk & 3) * 2);
-          const uint64_t aq = dq0 + kin + (kk >= 4 ? 1024u : 0u);
-          const uint64_t hk = kk >= 4 ? rh : 0;
-          mma_f16_ss_warp(dS, aq, dk1 + kin + hk, id1, kk > 0);
-          if (n2 > 0) mma_f16_ss_warp(dS + (uint32_t)n1, aq, dk2 + kin + hk, id2, kk > 0);
-          mma_f16_ss_warp(dS + (uint32_t)NR, aq, ds0 + kin + (kk >= 4 ? 128u : 0u), id_qs, kk > 0);
+          mma_f16_ss_warp(dS, dq0 + kin + (kk >= 4 ? 1024u : 0u), dk0 + kin + (kk >= 4 ? kh : 0), id_qk, kk > 0);
         }
         mma_commit_warp(&sfull[g]);
         mma_commit_warp(&qkdone[i & 3]);
-        return true;
       };
-      auto issue_pv = [&](int i) -> bool {
-        const int g = i & 1, k3 = i % 3;
+      auto issue_pv = [&](int i) {
+        const int g = i & 1;
         tc_fence_after();
         fence_proxy_async_smem();
         if (lane == 0) stamp(i, 4);
-        const uint32_t vb = smem_u32(smem + L.vring);
-        const uint32_t vs = smem_u32(smem + L.vsum + (uint32_t)k3 * 4096u);
+        const uint32_t vs = smem_u32(smem + L.vsum + (uint32_t)(i % 3) * 4096u);
         const uint32_t aP = tmem + (uint32_t)g * 128u;
         const uint32_t dO = tmem + 256u + (uint32_t)g * 128u;
         const int r0 = roff(i);
-        const uint64_t dv0 = desc_sw128(vb, L.ring_half, 1024);  // + row * 128 B per key step
-#pragma unroll 1
+        const uint64_t dv0 = desc_sw128(smem_u32(smem + L.vring), L.ring_half, 1024);  // + row * 128 B
+#pragma unroll
         for (int ks = 0; ks < NR / 16; ++ks) {
           int row = r0 + ks * 16;
           if (row >= R) row -= R;
@@ -313,43 +322,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_f16_ts_warp(dO, aP + (uint32_t)(NR / 16) * 8u, desc_sw128(vs, 2048, 1024), id_pv, 1);
         mma_commit_warp(&pvdone[i & 3]);
-        return true;
       };
-      // Issue whichever is ready (PV preferred): PV(j) once group j%2 stored P(j) and V(j)
-      // landed; QK(j) once Q(j) and K(j) landed and PV(j-2) (same S/P tile) completed.
-      auto ready = [&](uint64_t* bar, uint32_t parity) -> bool {
-        const bool r = lane == 0 ? mbar_test_wait(bar, parity) : false;
-        return __shfl_sync(0xffffffffu, r ? 1 : 0, 0) != 0;
-      };
-      int next_qk = 0, next_pv = 0;
-      int64_t last = clock64();
-      uint32_t spins = 0;
-      while (next_pv < n && ok) {
-        bool progressed = false;
-        if (next_pv < next_qk && ready(&pfull[next_pv & 1], (uint32_t)(next_pv >> 1) & 1u) &&
-            ready(&vfull[next_pv % 3], (uint32_t)(next_pv / 3) & 1u)) {
-          ok = issue_pv(next_pv++);
-          progressed = true;
-        } else if (next_qk < n && next_qk < next_pv + 2 &&
-                   (next_qk < 2 ||
-                    ready(&pvdone[(next_qk - 2) & 3], (uint32_t)((next_qk - 2) >> 2) & 1u)) &&
-                   ready(&qfull[next_qk % QS], (uint32_t)(next_qk / QS) & 1u) &&
-                   ready(&kfull[next_qk % 3], (uint32_t)(next_qk / 3) & 1u)) {
-          ok = issue_qk(next_qk++);
-          progressed = true;
+      for (int p = -2; p < n; ++p) {
+        if (p >= 0) {  // PV(p): P(p) stored by its group, V rows and summaries landed
+          if (!wait_all(&pfull[p & 1], (uint32_t)(p >> 1) & 1u, 7)) break;
+          if (!wait_all(&vfull[p % 3], (uint32_t)(p / 3) & 1u, 7)) break;
+          issue_pv(p);
         }
-        if (progressed) {
-          spins = 0;
-          last = clock64();
-        } else if ((++spins & 255) == 0) {
-          if (__shfl_sync(0xffffffffu, *abort_flag, 0)) break;
-          if (__shfl_sync(0xffffffffu, (clock64() - last > kWaitTimeoutCycles) ? 1 : 0, 0)) {
-            if (lane == 0) {
-              *abort_flag = 1;
-              if (a.err) atomicCAS(a.err, 0, 0x1000 | 8);
-            }
-            break;
-          }
+        const int j = p + 2;
+        if (j < n) {  // QK(j): S/P tile of PV(j - 2) free, Q and K landed
+          if (j >= 2 && !wait_all(&pvdone[(j - 2) & 3], (uint32_t)((j - 2) >> 2) & 1u, 8)) break;
+          if (!wait_all(&qfull[j % QS], (uint32_t)(j / QS) & 1u, 8)) break;
+          if (!wait_all(&kfull[j % kKSlots], (uint32_t)(j / kKSlots) & 1u, 8)) break;
+          issue_qk(j);
         }
       }
       volatile int never_abort = 0;
@@ -390,7 +375,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int kstart = a.q_pos0_i + qs - (a.window - 1);
       const int lo = max(0, qglob - a.window + 1) - kstart;
       const int hi = qglob - kstart;
-      if (row == 0 && half == 0) stamp(i, 13);
       if (!mbar_wait(&sfull[grp], par, abort_flag, 4, a.err)) break;
       // routed-summary count of this unit, published by the producer (tagged word)
       int ns = 0;
@@ -406,39 +390,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t wspan = valid_row ? (uint32_t)(hi - lo) : 0u;
       const int nsv = valid_row ? ns : 0;
 
-      // S columns of my half in registers; masked entries become -inf.
-      constexpr int kMaxCols = kHalf0 > NK_ - kHalf0 ? kHalf0 : NK_ - kHalf0;
-      const int cbeg = half ? kHalf0 : 0;
-      float x[kMaxCols];
-      float mp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      if (half == 0) {
+      // S columns of my half in registers; masked entries become -inf.  The half is a
+      // compile-time constant inside `soft`, so column indices and their window / summary
+      // tests fold to immediates.
+      float lp[4] = {0.f, 0.f, 0.f, 0.f};
+      float mb = 0.f;
+      auto soft = [&](auto half_c) {
+        constexpr int H = decltype(half_c)::value;
+        constexpr int CB = H ? kHalf0 : 0, CE = H ? NK_ : kHalf0, NC = CE - CB;
+        float x[NC];
+        float mp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int c0 = 0; c0 < kHalf0; c0 += 16) tmem_ld16(tS + c0, x + c0);
-      } else {
+        for (int c0 = CB; c0 < CE; c0 += 16) tmem_ld16(tS + c0, x + (c0 - CB));
+        tmem_ld_wait();
 #pragma unroll
-        for (int c0 = kHalf0; c0 < NK_; c0 += 16) tmem_ld16(tS + c0, x + (c0 - kHalf0));
-      }
-      tmem_ld_wait();
-#pragma unroll
-      for (int k = 0; k < kMaxCols; ++k) {
-        const int c = cbeg + k;  // uniform per warp
-        if (c < NK_) {
+        for (int k = 0; k < NC; ++k) {
+          const int c = CB + k;
           const bool v = c < NR_ ? ((uint32_t)c - wlo <= wspan) : (c - NR_ < nsv);
           x[k] = v ? x[k] : -INFINITY;
           mp[k & 3] = fmaxf(mp[k & 3], x[k]);
         }
-      }
-      float m = fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3]));
-      xm[row] = m;
-      named_bar_sync(bar_id, 64);
-      m = fmaxf(m, xo[row]);
-      const float mb = m > -INFINITY ? m * sl2 : 0.f;
-
-      float lp[4] = {0.f, 0.f, 0.f, 0.f};
+        float m = fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3]));
+        xm[row] = m;
+        named_bar_sync(bar_id, 64);
+        m = fmaxf(m, xo[row]);
+        mb = m > -INFINITY ? m * sl2 : 0.f;
 #pragma unroll
-      for (int k0 = 0; k0 < kMaxCols; k0 += 16) {
-        const int c0 = cbeg + k0;
-        if (c0 < NK_ && (half == 1 || c0 < kHalf0)) {
+        for (int k0 = 0; k0 < NC; k0 += 16) {
           uint32_t pk[8];
 #pragma unroll
           for (int j = 0; j < 16; j += 2) {
@@ -447,9 +425,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             lp[(j >> 1) & 3] += p0 + p1;
             pk[j >> 1] = ElemTraits<T>::pack2_fast(p0, p1);
           }
-          tmem_st8(tS + (uint32_t)(c0 >> 1), pk);
+          tmem_st8(tS + (uint32_t)((CB + k0) >> 1), pk);
         }
-      }
+      };
+      if (half == 0) soft(std::integral_constant<int, 0>{});
+      else soft(std::integral_constant<int, 1>{});
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&pfull[grp]);
@@ -470,15 +450,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c0 = 0; c0 < 64; c0 += 16) tmem_ld16(tO + half * 64 + c0, o + c0);
         tmem_ld_wait();
+
         if (valid_row) {
 #pragma unroll
-          for (int c0 = 0; c0 < 64; c0 += 8) {
-            uint4 w;
-            w.x = ElemTraits<T>::pack2_fast(o[c0] * inv, o[c0 + 1] * inv);
-            w.y = ElemTraits<T>::pack2_fast(o[c0 + 2] * inv, o[c0 + 3] * inv);
-            w.z = ElemTraits<T>::pack2_fast(o[c0 + 4] * inv, o[c0 + 5] * inv);
-            w.w = ElemTraits<T>::pack2_fast(o[c0 + 6] * inv, o[c0 + 7] * inv);
-            st_128(orow + c0 * 2, w);
+          for (int c0 = 0; c0 < 64; c0 += 16) {
+            uint32_t w[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) w[j] = ElemTraits<T>::pack2_fast(o[c0 + 2 * j] * inv, o[c0 + 2 * j + 1] * inv);
+            if (a.o_st256) {
+              st_256(orow + c0 * 2, w);
+            } else {
+              st_128(orow + c0 * 2, make_uint4(w[0], w[1], w[2], w[3]));
+              st_128(orow + c0 * 2 + 16, make_uint4(w[4], w[5], w[6], w[7]));
+            }
           }
         }
       }
@@ -587,6 +571,8 @@ int launch_prefill(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4
   a.vs_b = vs->stride[0]; a.vs_h = vs->stride[1]; a.vs_n = vs->stride[2];
   a.out = out->data;
   a.os_b = out->stride[0]; a.os_h = out->stride[1]; a.os_t = out->stride[2];
+  a.o_st256 = (reinterpret_cast<uintptr_t>(out->data) % 32 == 0) && (a.os_b * 2) % 32 == 0 &&
+              (a.os_h * 2) % 32 == 0 && (a.os_t * 2) % 32 == 0;
   a.lse = lse;
   a.ls_b = ls_b;
   a.ls_h = ls_h;
@@ -621,9 +607,10 @@ int launch_prefill(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4
   }
   if (rc) return rc;
   const int okv[3] = {2, 1, 0};
-  const uint32_t bkv[3] = {16, 1, 1};  // ring loads in 16-row boxes
-  if ((rc = encode_map(&mk, k, dt, okv, bkv, "k"))) return rc;
-  if ((rc = encode_map(&mv, v, dt, okv, bkv, "v"))) return rc;
+  const uint32_t bk[3] = {(uint32_t)a.NR, 1, 1};  // a tile's whole key window
+  const uint32_t bv[3] = {16, 1, 1};              // V ring loads in 16-row boxes
+  if ((rc = encode_map(&mk, k, dt, okv, bk, "k"))) return rc;
+  if ((rc = encode_map(&mv, v, dt, okv, bv, "v"))) return rc;
 
   const int grid = a.total_units < nsm ? a.total_units : nsm;
   auto launch = [&](auto kern) {
