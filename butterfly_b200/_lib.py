@@ -99,15 +99,13 @@ def dtype_code(dt: torch.dtype) -> int:
     raise ValueError(f"compressed attention kernels take bfloat16 or float16 tensors, got {dt}")
 
 
+_I64x4 = ctypes.c_int64 * 4
+
+
 def t4(x: torch.Tensor) -> Tensor4:
     if x.dim() != 4:
         raise ValueError(f"expected a 4-D tensor, got shape {tuple(x.shape)}")
-    t = Tensor4()
-    t.data = x.data_ptr()
-    for i in range(4):
-        t.size[i] = int(x.shape[i])
-        t.stride[i] = int(x.stride(i))
-    return t
+    return Tensor4(x.data_ptr(), _I64x4(*x.shape), _I64x4(*x.stride()))
 
 
 def stream_ptr(device: torch.device) -> int:

@@ -16,6 +16,13 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// max of three floats in one instruction (sm_100 three-input max.f32)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // Two fp32 -> packed bf16x2 with round-to-nearest-even, on the integer ALU pipe (keeps the
 // conversion work off the transcendental pipe that the softmax exponentials saturate).
 // Inputs are finite.

@@ -28,6 +28,8 @@
 //   warps 2..17   two softmax/epilogue groups of 8 warps (units alternate between them);
 //                 two warps share each TMEM lane quarter and split the columns
 // TMEM (512 columns): group g's S/P tile at [128g, 128g+128), its O tile at 256 + 128g.
+#include <map>
+#include <mutex>
 #include <type_traits>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -78,8 +80,8 @@ struct PrefillSmem {
     ring_half = R * 128;                // one 64-column half of the V ring
     vring = kslot + kKSlots * kslot_size;
     vsum = vring + 2 * ring_half;
-    xchg = vsum + 3 * 4096;             // [2 groups][2 buffers][2 halves][128] row maxima
-    bars = xchg + 4096;
+    xchg = vsum + 3 * 4096;             // [2 (max, sum)][2 tile parities][4 column quarters][128] floats
+    bars = xchg + 8192;
     total = bars + 512 + 1024;          // + alignment slack
   }
 };
@@ -113,8 +115,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* vfull = bars + 7;    // [3] new V rows + V summary tile of unit i landed
   uint64_t* qkdone = bars + 10;  // [4] QK(i) complete (ring i % 4)
   uint64_t* pvdone = bars + 14;  // [4] PV(i) complete: O ready, V rows / summary tile free
-  uint64_t* sfull = bars + 18;   // [2] per group: S ready in TMEM
-  uint64_t* pfull = bars + 20;   // [2] per group: P stored in TMEM (256 arrivals)
+  uint64_t* sfull = bars + 18;   // [2] per S/P tile (unit parity): S ready in TMEM
+  uint64_t* pfull = bars + 20;   // [2] per S/P tile: P stored in TMEM (512 arrivals)
   uint64_t* drain = bars + 22;   // MMA drain at exit
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 23);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 24);
@@ -132,7 +134,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < 3; ++s) mbar_init(&vfull[s], 34);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sfull[s], 1);
-      mbar_init(&pfull[s], 256);
+      mbar_init(&pfull[s], 512);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -344,28 +346,67 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
-    // Group grp handles local units i with i % 2 == grp.  Its 8 warps pair up per TMEM lane
-    // quarter: half 0 takes S columns [0, kHalf0) and O columns [0, 64), half 1 the rest.
-    // The two threads of a row exchange partial max / sum through shared memory, synced
-    // by a 64-thread named barrier per (group, quarter).
-    constexpr int kHalf0 = ((NK_ / 16 + 1) / 2) * 16;
-    const int gw = warp - 2;
-    const int grp = gw >> 3;
-    const int half = (gw >> 2) & 1;
-    const int quad = warp & 3;  // TMEM lane quarter this warp may access
+    // All 16 warps work on every unit.  Warp w may read TMEM lane quarter w % 4 (its rows);
+    // the four warps of a quarter split the row's columns: S in 8-column chunks, O in 32
+    // columns each.  The warps of one SM sub-partition thus run the same code together.
+    // Row maxima are exchanged through shared memory under a 128-thread named barrier per
+    // quarter; the epilogue of unit i - 1 runs after the softmax of unit i, so the P.V
+    // product of a unit overlaps the next unit's softmax.
+    constexpr int NCH = NK_ / 8;          // 8-column S chunks
+    constexpr int MC = (NCH + 3) / 4;     // most chunks of one column quarter
+    const int sw = warp - 2;
+    const int cq = sw >> 2;               // column quarter
+    const int quad = warp & 3;            // TMEM lane quarter this warp may access
     const int row = quad * 32 + lane;
+    const int chb = cq * NCH / 4, chn = (cq + 1) * NCH / 4 - chb;  // my S chunks
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t tS = tmem + lane_off + (uint32_t)grp * 128u;
-    const uint32_t tO = tmem + lane_off + 256u + (uint32_t)grp * 128u;
     const int g = a.q_tmajor ? (row % G) : (row / QT);
     const int qi = a.q_tmajor ? (row / G) : (row % QT);
-    float* xm = xchg + (grp * 2 + half) * 256;        // my partial max [0,128) / sum [128,256)
-    float* xo = xchg + (grp * 2 + (half ^ 1)) * 256;  // partner's
-    const uint32_t bar_id = 1u + (uint32_t)(grp * 4 + quad);
+    float* pmax = xchg;                   // [2][4][128]
+    float* psum = xchg + 1024;            // [2][4][128]
+    const uint32_t bar_id = 1u + (uint32_t)quad;
     const float sl2 = a.scale_log2;
-    for (int i = grp; i < n_units; i += 2) {
+    // epilogue state of the previous unit
+    int e_b = 0, e_kvh = 0, e_qloc = 0;
+    bool e_valid = false;
+    float e_mb = 0.f;
+    auto epilogue = [&](int i) -> bool {
+      if (!mbar_wait(&pvdone[i & 3], (uint32_t)(i >> 2) & 1u, abort_flag, 5, a.err)) return false;
+      if (row == 0 && cq == 0) stamp(i, 7);
+      tc_fence_after();
+      const float* ps = psum + (i & 1) * 512 + row;
+      const float l = (ps[0] + ps[128]) + (ps[256] + ps[384]);
+      const float inv = (e_valid && l > 0.f) ? 1.f / l : 0.f;
+      float o[32];
+      const uint32_t tO = tmem + lane_off + 256u + (uint32_t)(i & 1) * 128u + (uint32_t)cq * 32u;
+      tmem_ld16(tO, o);
+      tmem_ld16(tO + 16, o + 16);
+      tmem_ld_wait();
+      if (e_valid) {
+        uint8_t* orow = reinterpret_cast<uint8_t*>(a.out) +
+                        2 * (e_b * a.os_b + (int64_t)(e_kvh * G + g) * a.os_h + (int64_t)e_qloc * a.os_t) + cq * 64;
+#pragma unroll
+        for (int c0 = 0; c0 < 32; c0 += 16) {
+          uint32_t w[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) w[j] = ElemTraits<T>::pack2_fast(o[c0 + 2 * j] * inv, o[c0 + 2 * j + 1] * inv);
+          if (a.o_st256) {
+            st_256(orow + c0 * 2, w);
+          } else {
+            st_128(orow + c0 * 2, make_uint4(w[0], w[1], w[2], w[3]));
+            st_128(orow + c0 * 2 + 16, make_uint4(w[4], w[5], w[6], w[7]));
+          }
+        }
+        if (a.lse && cq == 0)
+          a.lse[e_b * a.ls_b + (int64_t)(e_kvh * G + g) * a.ls_h + e_qloc] = (e_mb + log2f(l)) * kLn2;
+      }
+      if (row == 0 && cq == 0) stamp(i, 8);
+      tc_fence_before();
+      return true;
+    };
+    bool ok = true;
+    for (int i = 0; i < n_units && ok; ++i) {
       const int u = u_begin + i;
-      const uint32_t par = (uint32_t)(i >> 1) & 1u;
       const int t = u % a.ntiles, rest = u / a.ntiles, kvh = rest % a.Hkv, b = rest / a.Hkv;
       const int qs = t * QT;
       const int qloc = qs + qi;
@@ -375,7 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int kstart = a.q_pos0_i + qs - (a.window - 1);
       const int lo = max(0, qglob - a.window + 1) - kstart;
       const int hi = qglob - kstart;
-      if (!mbar_wait(&sfull[grp], par, abort_flag, 4, a.err)) break;
+      if (!mbar_wait(&sfull[i & 1], (uint32_t)(i >> 1) & 1u, abort_flag, 4, a.err)) break;
       // routed-summary count of this unit, published by the producer (tagged word)
       int ns = 0;
       {
@@ -384,93 +425,77 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int spin = 0; (w >> 8) != (uint32_t)i && spin < (1 << 22); ++spin) w = *slot;
         ns = (int)(w & 0xFFu);
       }
-      if (row == 0 && half == 0) stamp(i, 5);
+      if (row == 0 && cq == 0) stamp(i, 5);
       tc_fence_after();
       const uint32_t wlo = valid_row ? (uint32_t)lo : 1u;
       const uint32_t wspan = valid_row ? (uint32_t)(hi - lo) : 0u;
       const int nsv = valid_row ? ns : 0;
+      const uint32_t tS = tmem + lane_off + (uint32_t)(i & 1) * 128u;
 
-      // S columns of my half in registers; masked entries become -inf.  The half is a
-      // compile-time constant inside `soft`, so column indices and their window / summary
-      // tests fold to immediates.
-      float lp[4] = {0.f, 0.f, 0.f, 0.f};
-      float mb = 0.f;
-      auto soft = [&](auto half_c) {
-        constexpr int H = decltype(half_c)::value;
-        constexpr int CB = H ? kHalf0 : 0, CE = H ? NK_ : kHalf0, NC = CE - CB;
-        float x[NC];
-        float mp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      // my S chunks in registers; masked entries become -inf
+      float x[MC * 8];
 #pragma unroll
-        for (int c0 = CB; c0 < CE; c0 += 16) tmem_ld16(tS + c0, x + (c0 - CB));
-        tmem_ld_wait();
+      for (int j = 0; j < MC; ++j)
+        if (j < chn) tmem_ld8(tS + (uint32_t)(chb + j) * 8u, x + j * 8);
+      tmem_ld_wait();
+      float mp[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-        for (int k = 0; k < NC; ++k) {
-          const int c = CB + k;
-          const bool v = c < NR_ ? ((uint32_t)c - wlo <= wspan) : (c - NR_ < nsv);
-          x[k] = v ? x[k] : -INFINITY;
-          mp[k & 3] = fmaxf(mp[k & 3], x[k]);
-        }
-        float m = fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3]));
-        xm[row] = m;
-        named_bar_sync(bar_id, 64);
-        m = fmaxf(m, xo[row]);
-        mb = m > -INFINITY ? m * sl2 : 0.f;
+      for (int j = 0; j < MC; ++j) {
+        if (j < chn) {
+          const int c0 = (chb + j) * 8;  // chunks never straddle the window / summary boundary
+          if (c0 < NR_) {
+            const uint32_t d0 = (uint32_t)c0 - wlo;
 #pragma unroll
-        for (int k0 = 0; k0 < NC; k0 += 16) {
-          uint32_t pk[8];
+            for (int e = 0; e < 8; ++e) x[j * 8 + e] = (d0 + (uint32_t)e <= wspan) ? x[j * 8 + e] : -INFINITY;
+          } else {
+            const int s0 = c0 - NR_;
 #pragma unroll
-          for (int j = 0; j < 16; j += 2) {
-            const float p0 = ex2_approx(fmaf(x[k0 + j], sl2, -mb));
-            const float p1 = ex2_approx(fmaf(x[k0 + j + 1], sl2, -mb));
-            lp[(j >> 1) & 3] += p0 + p1;
-            pk[j >> 1] = ElemTraits<T>::pack2_fast(p0, p1);
+            for (int e = 0; e < 8; ++e) x[j * 8 + e] = (s0 + e < nsv) ? x[j * 8 + e] : -INFINITY;
           }
-          tmem_st8(tS + (uint32_t)((CB + k0) >> 1), pk);
-        }
-      };
-      if (half == 0) soft(std::integral_constant<int, 0>{});
-      else soft(std::integral_constant<int, 1>{});
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&pfull[grp]);
-      if (row == 0 && half == 0) stamp(i, 6);
-      float l = (lp[0] + lp[1]) + (lp[2] + lp[3]);
-      xm[128 + row] = l;
-      named_bar_sync(bar_id, 64);
-      l += xo[128 + row];
-
-      if (!mbar_wait(&pvdone[i & 3], (uint32_t)(i >> 2) & 1u, abort_flag, 5, a.err)) break;
-      if (row == 0 && half == 0) stamp(i, 7);
-      tc_fence_after();
-      const float inv = (valid_row && l > 0.f) ? 1.f / l : 0.f;
-      uint8_t* orow = reinterpret_cast<uint8_t*>(a.out) +
-                      2 * (b * a.os_b + (int64_t)(kvh * G + g) * a.os_h + (int64_t)qloc * a.os_t) + half * 128;
-      {
-        float o[64];
 #pragma unroll
-        for (int c0 = 0; c0 < 64; c0 += 16) tmem_ld16(tO + half * 64 + c0, o + c0);
-        tmem_ld_wait();
-
-        if (valid_row) {
-#pragma unroll
-          for (int c0 = 0; c0 < 64; c0 += 16) {
-            uint32_t w[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) w[j] = ElemTraits<T>::pack2_fast(o[c0 + 2 * j] * inv, o[c0 + 2 * j + 1] * inv);
-            if (a.o_st256) {
-              st_256(orow + c0 * 2, w);
-            } else {
-              st_128(orow + c0 * 2, make_uint4(w[0], w[1], w[2], w[3]));
-              st_128(orow + c0 * 2 + 16, make_uint4(w[4], w[5], w[6], w[7]));
-            }
+          for (int e = 0; e < 8; e += 4) {
+            mp[0] = fmax3(mp[0], x[j * 8 + e], x[j * 8 + e + 1]);
+            mp[1] = fmax3(mp[1], x[j * 8 + e + 2], x[j * 8 + e + 3]);
           }
         }
       }
-      if (valid_row && a.lse && half == 0)
-        a.lse[b * a.ls_b + (int64_t)(kvh * G + g) * a.ls_h + qloc] = (mb + log2f(l)) * kLn2;
-      if (row == 0 && half == 0) stamp(i, 8);
+      pmax[(i & 1) * 512 + cq * 128 + row] = fmaxf(mp[0], mp[1]);
+      named_bar_sync(bar_id, 128);
+      const float* pm = pmax + (i & 1) * 512 + row;
+      const float m = fmaxf(fmaxf(pm[0], pm[128]), fmaxf(pm[256], pm[384]));
+      const float mb = m > -INFINITY ? m * sl2 : 0.f;
+      float lp[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < MC; ++j) {
+        if (j < chn) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            const float p0 = ex2_approx(fmaf(x[j * 8 + e], sl2, -mb));
+            const float p1 = ex2_approx(fmaf(x[j * 8 + e + 1], sl2, -mb));
+            lp[e >> 1] += p0 + p1;
+            pk[e >> 1] = ElemTraits<T>::pack2_fast(p0, p1);
+          }
+          tmem_st4(tS + (uint32_t)(chb + j) * 4u, pk);  // P column = S column / 2
+        }
+      }
+      tmem_st_wait();
       tc_fence_before();
+      mbar_arrive(&pfull[i & 1]);
+      if (row == 0 && cq == 0) stamp(i, 6);
+      psum[(i & 1) * 512 + cq * 128 + row] = (lp[0] + lp[1]) + (lp[2] + lp[3]);
+      // output of the previous unit (its partial sums were published before this unit's
+      // max-exchange barrier)
+      if (i > 0) ok = epilogue(i - 1);
+      e_b = b;
+      e_kvh = kvh;
+      e_qloc = qloc;
+      e_valid = valid_row;
+      e_mb = mb;
     }
+    // the last unit's partial sums: every thread of the quarter must have written them
+    named_bar_sync(bar_id, 128);
+    if (ok && n_units > 0) epilogue(n_units - 1);
   }
   tc_fence_before();
   __syncthreads();
@@ -494,6 +519,33 @@ int launch_prefill_staged(const bna_tensor4*, const bna_tensor4*, const bna_tens
 // bna_set_prefill_trace; nullptr disables the stamps.
 static uint64_t* g_prefill_trace = nullptr;
 void set_prefill_trace(uint64_t* p) { g_prefill_trace = p; }
+// Per-device limits and per-(kernel, device) shared-memory opt-in, looked up once: they
+// are host-side costs on every call otherwise.
+struct DeviceLimits {
+  int nsm, max_smem;
+};
+static DeviceLimits device_limits(int dev) {
+  static std::mutex mu;
+  static std::map<int, DeviceLimits> cache;
+  std::lock_guard<std::mutex> g(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  DeviceLimits d{0, 0};
+  cudaDeviceGetAttribute(&d.nsm, cudaDevAttrMultiProcessorCount, dev);
+  cudaDeviceGetAttribute(&d.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  cache[dev] = d;
+  return d;
+}
+static void set_smem_limit_once(const void* fn, int dev, int smem) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;  // largest limit set so far
+  std::lock_guard<std::mutex> g(mu);
+  int& cur = done[{fn, dev}];
+  if (cur >= smem) return;
+  cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cur = smem;
+}
+
 using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
 
 static EncodeFn get_encode() {
@@ -580,10 +632,10 @@ int launch_prefill(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4
   a.trace = g_prefill_trace;
 
 
-  int dev = 0, nsm = 0, max_smem = 0;
+  int dev = 0;
   cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  const DeviceLimits lim = device_limits(dev);
+  const int nsm = lim.nsm, max_smem = lim.max_smem;
   a.QS = 3;
   if ((int)PrefillSmem(a.NR, a.QT, 3).total > max_smem) a.QS = 2;
   const uint32_t smem = PrefillSmem(a.NR, a.QT, a.QS).total;
@@ -614,7 +666,7 @@ int launch_prefill(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4
 
   const int grid = a.total_units < nsm ? a.total_units : nsm;
   auto launch = [&](auto kern) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    set_smem_limit_once(reinterpret_cast<const void*>(kern), dev, (int)smem);
     kern<<<grid, kThreads, smem, stream>>>(mq, mk, mv, a);
   };
 #define BNA_PREFILL_CASE(NRV)                                          \
