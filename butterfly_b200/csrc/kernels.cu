@@ -204,6 +204,20 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const ActiveArgs
     }
     cp_async_16(kv + (isv * maxk + j) * kRow + ch * 16, src + ch * 16);
   }
+  // host-routed summaries of a step that closes no block: their rows load together with
+  // the window rows, in the same round trip (a block closed in this step is written below
+  // and may be routed, so such steps load the summaries after the close)
+  const bool early_sum = a.host_ns >= 0 && a.close_block < 0;
+  if (early_sum) {
+#pragma unroll 1
+    for (int c = threadIdx.x; c < 2 * a.host_ns * 16; c += kDecodeThreads) {
+      const int isv = c >= a.host_ns * 16;
+      const int e = isv ? c - a.host_ns * 16 : c;
+      const int j = e >> 4, ch = e & 15;
+      cp_async_16(kv + (isv * maxk + nraw + j) * kRow + ch * 16,
+                  row_ptr(isv ? a.vs : a.ks, b, kvh, a.host_ids[j]) + ch * 16);
+    }
+  }
   if (a.knew && threadIdx.x < 32) {  // fused append of the new token into ring slot p % ring
     const int slot = (int)((uint64_t)p % (uint64_t)a.ring);
     const bool isv = threadIdx.x >= 16;
@@ -238,7 +252,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const ActiveArgs
   const int ns = sel[0];
   const int nk = nraw + ns;
 #pragma unroll 1
-  for (int c = threadIdx.x; c < 2 * ns * 16; c += kDecodeThreads) {
+  for (int c = early_sum ? 2 * ns * 16 : threadIdx.x; c < 2 * ns * 16; c += kDecodeThreads) {
     const int isv = c >= ns * 16;
     const int e = isv ? c - ns * 16 : c;
     const int j = e >> 4, ch = e & 15;
