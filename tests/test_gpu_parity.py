@@ -110,6 +110,29 @@ def test_prefill_hf_transposed_views_fp16_and_table():
     _check_prefill(1, 8, 2, 1200, 128, 64, 3, foreign_table=True)
 
 
+def test_prefill_output_store_paths_agree_bitwise():
+    # an output view whose rows are 16- but not 32-byte aligned takes the 128-bit store path;
+    # it must write exactly what the 256-bit path writes into a contiguous output
+    from butterfly_b200.attention import block_mean_summaries, prefill_attention_into, route_for
+    B, Hq, Hkv, T, BS, W = 1, 8, 2, 4096, 128, 64
+    q, k, v = _inputs(B, Hq, Hkv, T, 128, 7)
+    lay = _layout(T, BS, Hkv, Hq // Hkv, 4)
+    route, _keep = route_for(lay, q.device)
+    N = lay.num_blocks
+    ks = block_mean_summaries(k, seq_len=T, block_size=BS, num_blocks=N)
+    vs = block_mean_summaries(v, seq_len=T, block_size=BS, num_blocks=N)
+    sc = 1.0 / math.sqrt(128)
+    out_a = torch.empty(B, T, Hq, 128, device=q.device, dtype=q.dtype).transpose(1, 2)
+    big = torch.zeros(B, T, Hq, 136, device=q.device, dtype=q.dtype)
+    out_b = big[..., 8:].transpose(1, 2)  # head stride 136 * 2 B: not a 32-byte multiple
+    assert (out_b.stride(1) * 2) % 32 != 0 and (out_b.data_ptr() % 16) == 0
+    prefill_attention_into(q, k, v, ks, vs, out_a, None, route, W, sc)
+    prefill_attention_into(q, k, v, ks, vs, out_b, None, route, W, sc)
+    torch.cuda.synchronize()
+    assert torch.equal(out_a, out_b)
+    assert torch.count_nonzero(big[..., :8]) == 0  # nothing written outside the view
+
+
 def test_selection_device_equals_host():
     import ctypes
     for T, layer, rule in [(32768, 5, "causal_shift"), (4096, 3, "causal_shift"), (70000, 9, "xor")]:
