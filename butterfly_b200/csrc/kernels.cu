@@ -152,8 +152,13 @@ struct ActiveArgs {
   int host_ids[kMaxSummaries];
 };
 
-constexpr int kDecodeThreads = 256;
+constexpr int kDecodeThreads = 512;
 constexpr int kDecodeWarps = kDecodeThreads / 32;
+constexpr int kKeyParts = kDecodeThreads / 64;  // P.V key ranges summed through shared memory
+// reduction buffer (floats): block-mean partials or the P.V partial sums
+__host__ __device__ constexpr int decode_red_floats(int G) {
+  return kDecodeThreads * 8 > kKeyParts * 128 * G ? kDecodeThreads * 8 : kKeyParts * 128 * G;
+}
 
 __device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
@@ -171,7 +176,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const ActiveArgs
   float* sc = reinterpret_cast<float*>(kv + 2 * maxk * kRow);      // [G][maxk] scores -> weights
   float* qs = sc + G * maxk;                                       // [G][128] scaled queries
   float* red = qs + G * 128;                                       // [256 * 8] block-mean reduction
-  constexpr int kRed = kDecodeThreads * 8 > 512 * G ? kDecodeThreads * 8 : 512 * G;
+  constexpr int kRed = decode_red_floats(G);
   float* stat = red + kRed;                                        // [G] row sums
   int* sel = reinterpret_cast<int*>(stat + G);                     // [1 + 16] summary count + ids
 
@@ -305,17 +310,17 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const ActiveArgs
     }
   }
   __syncthreads();
-  // weighted values: thread = (key quarter, head, 2 columns); the 4 key quarters' partial
-  // sums meet in shared memory (reusing the block-mean buffer)
-  float* part = red;  // [4][G * 64][2]
+  // weighted values: thread = (key range, head, 2 columns); the kKeyParts key ranges'
+  // partial sums meet in shared memory (reusing the block-mean buffer)
+  float* part = red;  // [kKeyParts][G * 64][2]
   const int npairs = G * 64;
 #pragma unroll 1
-  for (int e = threadIdx.x; e < 4 * npairs; e += kDecodeThreads) {
+  for (int e = threadIdx.x; e < kKeyParts * npairs; e += kDecodeThreads) {
     const int qtr = e / npairs, r = e - qtr * npairs;
     const int g = r >> 6, c = (r & 63) * 2;
     const float* w = sc + g * maxk;
     const uint8_t* vb = kv + maxk * kRow + c * 2;
-    const int j0 = (nk * qtr) >> 2, j1 = (nk * (qtr + 1)) >> 2;
+    const int j0 = nk * qtr / kKeyParts, j1 = nk * (qtr + 1) / kKeyParts;
     float s0 = 0.f, s1 = 0.f;
 #pragma unroll 2
     for (int j = j0; j < j1; ++j) {
@@ -331,7 +336,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const ActiveArgs
     const int g = r >> 6, c = (r & 63) * 2;
     float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-    for (int qtr = 0; qtr < 4; ++qtr) {
+    for (int qtr = 0; qtr < kKeyParts; ++qtr) {
       const float2 f = *reinterpret_cast<const float2*>(part + 2 * (qtr * npairs + r));
       s0 += f.x;
       s1 += f.y;
@@ -424,7 +429,7 @@ int launch_active(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4*
   const int maxk = window + kMaxSummaries;
   const size_t smem = (size_t)2 * maxk * (256 + 16) +
                       sizeof(float) * ((size_t)a.G * maxk + (size_t)a.G * 128 +
-                                       (size_t)(kDecodeThreads * 8 > 512 * a.G ? kDecodeThreads * 8 : 512 * a.G) +
+                                       (size_t)decode_red_floats(a.G) +
                                        (size_t)a.G) +
                       sizeof(int) * (1 + kMaxSummaries);
   dim3 grid((unsigned)a.Tq, (unsigned)(a.B * a.Hkv));
