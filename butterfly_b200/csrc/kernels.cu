@@ -173,9 +173,11 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const ActiveArgs
   const int maxk = a.window + kMaxSummaries;
   constexpr int kRow = 256 + 16;                                   // padded staged row (bank spread)
   uint8_t* kv = dsm_raw;                                           // [2][maxk][kRow] K rows, V rows
-  float* sc = reinterpret_cast<float*>(kv + 2 * maxk * kRow);      // [G][maxk] scores -> weights
-  float* qs = sc + G * maxk;                                       // [G][128] scaled queries
-  float* red = qs + G * 128;                                       // [256 * 8] block-mean reduction
+  uint8_t* qraw = kv + 2 * maxk * kRow;                            // [G][256 B] queries as loaded
+  float* sc = reinterpret_cast<float*>(qraw + G * 256);            // [G][maxk] scores -> weights
+  constexpr int kQRow = 132;  // scaled query row stride (floats): rows of different heads in different banks
+  float* qs = sc + G * maxk;                                       // [G][kQRow] scaled queries
+  float* red = qs + G * kQRow;                                     // block-mean / P.V reduction
   constexpr int kRed = decode_red_floats(G);
   float* stat = red + kRed;                                        // [G] row sums
   int* sel = reinterpret_cast<int*>(stat + G);                     // [1 + 16] summary count + ids
@@ -231,12 +233,10 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const ActiveArgs
                          2 * (b * (isv ? a.vn_b : a.kn_b) + kvh * (isv ? a.vn_h : a.kn_h));
     st_128(row_ptr(isv ? a.v : a.k, b, kvh, slot) + ch * 16, ld_nc_128(src + ch * 16));
   }
-#pragma unroll 1
-  for (int c = threadIdx.x; c < G * 64; c += kDecodeThreads) {  // queries, scaled to log2 units
-    const int g = c >> 6, d = (c & 63) * 2;
-    const float2 f = ElemTraits<T>::unpack2(*reinterpret_cast<const uint32_t*>(row_ptr(a.q, b, kvh * G + g, t) + d * 2));
-    qs[g * 128 + d] = f.x * a.scale_log2;
-    qs[g * 128 + d + 1] = f.y * a.scale_log2;
+  // queries: raw rows in the same round trip as the keys and values, scaled below
+  for (int c = threadIdx.x; c < G * 16; c += kDecodeThreads) {
+    const int g = c >> 4, ch = c & 15;
+    cp_async_16(qraw + g * 256 + ch * 16, row_ptr(a.q, b, kvh * G + g, t) + ch * 16);
   }
   if (a.close_block >= 0) {  // fused block close: mean of the block's tokens from the ring
     const int BS = a.route.block_size;
@@ -266,13 +266,21 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const ActiveArgs
   }
   cp_async_wait_all();
   __syncthreads();
+#pragma unroll 1
+  for (int c = threadIdx.x; c < G * 64; c += kDecodeThreads) {  // queries, scaled to log2 units
+    const int g = c >> 6, d = (c & 63) * 2;
+    const float2 f = ElemTraits<T>::unpack2(*reinterpret_cast<const uint32_t*>(qraw + g * 256 + d * 2));
+    qs[g * kQRow + d] = f.x * a.scale_log2;
+    qs[g * kQRow + d + 1] = f.y * a.scale_log2;
+  }
+  __syncthreads();
 
   // scores: one thread per (key, head), full 128-wide dot from shared memory
 #pragma unroll 1
   for (int e = threadIdx.x; e < nk * G; e += kDecodeThreads) {
     const int j = e / G, g = e - j * G;
     const uint4* kr = reinterpret_cast<const uint4*>(kv + j * kRow);
-    const float4* q4 = reinterpret_cast<const float4*>(qs + g * 128);
+    const float4* q4 = reinterpret_cast<const float4*>(qs + g * kQRow);
     float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
 #pragma unroll 4
     for (int c = 0; c < 16; ++c) {
@@ -427,8 +435,8 @@ int launch_active(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4*
   a.close_block = close_block;
   a.close_slot = close_slot;
   const int maxk = window + kMaxSummaries;
-  const size_t smem = (size_t)2 * maxk * (256 + 16) +
-                      sizeof(float) * ((size_t)a.G * maxk + (size_t)a.G * 128 +
+  const size_t smem = (size_t)2 * maxk * (256 + 16) + (size_t)a.G * 256 +
+                      sizeof(float) * ((size_t)a.G * maxk + (size_t)a.G * 132 +
                                        (size_t)decode_red_floats(a.G) +
                                        (size_t)a.G) +
                       sizeof(int) * (1 + kMaxSummaries);
