@@ -182,6 +182,11 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const ActiveArgs
   float* stat = red + kRed;                                        // [G] row sums
   int* sel = reinterpret_cast<int*>(stat + G);                     // [1 + 16] summary count + ids
 
+  // Launched with programmatic stream serialization: this grid may start while the previous
+  // kernel of the stream finishes; wait for it (and its memory) before touching anything,
+  // then let the next step's grid start launching.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int t = blockIdx.x;
   const int b = blockIdx.y / a.Hkv, kvh = blockIdx.y % a.Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -225,14 +230,6 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const ActiveArgs
                   row_ptr(isv ? a.vs : a.ks, b, kvh, a.host_ids[j]) + ch * 16);
     }
   }
-  if (a.knew && threadIdx.x < 32) {  // fused append of the new token into ring slot p % ring
-    const int slot = (int)((uint64_t)p % (uint64_t)a.ring);
-    const bool isv = threadIdx.x >= 16;
-    const int ch = threadIdx.x & 15;
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(isv ? a.vnew : a.knew) +
-                         2 * (b * (isv ? a.vn_b : a.kn_b) + kvh * (isv ? a.vn_h : a.kn_h));
-    st_128(row_ptr(isv ? a.v : a.k, b, kvh, slot) + ch * 16, ld_nc_128(src + ch * 16));
-  }
   // queries: raw rows in the same round trip as the keys and values, scaled below
   for (int c = threadIdx.x; c < G * 16; c += kDecodeThreads) {
     const int g = c >> 4, ch = c & 15;
@@ -266,6 +263,15 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const ActiveArgs
   }
   cp_async_wait_all();
   __syncthreads();
+  if (a.knew && threadIdx.x < 32) {
+    // fused append: the new token (staged as the last window row) goes to ring slot
+    // p % ring; any block close above has already read the ring
+    const int slot = (int)((uint64_t)p % (uint64_t)a.ring);
+    const int isv = threadIdx.x >= 16;
+    const int ch = threadIdx.x & 15;
+    st_128(row_ptr(isv ? a.v : a.k, b, kvh, slot) + ch * 16,
+           *reinterpret_cast<const uint4*>(kv + (isv * maxk + nraw - 1) * kRow + ch * 16));
+  }
 #pragma unroll 1
   for (int c = threadIdx.x; c < G * 64; c += kDecodeThreads) {  // queries, scaled to log2 units
     const int g = c >> 6, d = (c & 63) * 2;
@@ -318,25 +324,38 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const ActiveArgs
     }
   }
   __syncthreads();
-  // weighted values: thread = (key range, head, 2 columns); the kKeyParts key ranges'
-  // partial sums meet in shared memory (reusing the block-mean buffer)
-  float* part = red;  // [kKeyParts][G * 64][2]
+  // weighted values: thread = (key range, head, 8 columns): one 16-byte V load and eight
+  // independent FMAs per key; the key ranges' partial sums meet in shared memory
+  // (reusing the block-mean buffer)
+  constexpr int kOct = G * 16;
+  constexpr int kParts = kDecodeThreads / kOct > 0 ? kDecodeThreads / kOct : 1;
+  float* part = red;  // [kParts][G * 128]
   const int npairs = G * 64;
 #pragma unroll 1
-  for (int e = threadIdx.x; e < kKeyParts * npairs; e += kDecodeThreads) {
-    const int qtr = e / npairs, r = e - qtr * npairs;
-    const int g = r >> 6, c = (r & 63) * 2;
+  for (int e = threadIdx.x; e < kParts * kOct; e += kDecodeThreads) {
+    const int pi = e / kOct, r = e - pi * kOct;
+    const int g = r >> 4, oc = r & 15;
     const float* w = sc + g * maxk;
-    const uint8_t* vb = kv + maxk * kRow + c * 2;
-    const int j0 = nk * qtr / kKeyParts, j1 = nk * (qtr + 1) / kKeyParts;
-    float s0 = 0.f, s1 = 0.f;
-#pragma unroll 2
+    const uint8_t* vb = kv + maxk * kRow + oc * 16;
+    const int j0 = nk * pi / kParts, j1 = nk * (pi + 1) / kParts;
+    float acc[8];
+#pragma unroll
+    for (int x = 0; x < 8; ++x) acc[x] = 0.f;
+#pragma unroll 4
     for (int j = j0; j < j1; ++j) {
-      const float2 f = ElemTraits<T>::unpack2(*reinterpret_cast<const uint32_t*>(vb + j * kRow));
-      s0 = fmaf(w[j], f.x, s0);
-      s1 = fmaf(w[j], f.y, s1);
+      const uint4 u = *reinterpret_cast<const uint4*>(vb + j * kRow);
+      const float wj = w[j];
+      const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        const float2 f = ElemTraits<T>::unpack2(uw[x]);
+        acc[2 * x] = fmaf(wj, f.x, acc[2 * x]);
+        acc[2 * x + 1] = fmaf(wj, f.y, acc[2 * x + 1]);
+      }
     }
-    *reinterpret_cast<float2*>(part + 2 * (qtr * npairs + r)) = make_float2(s0, s1);
+    float4* dst = reinterpret_cast<float4*>(part + pi * G * 128 + g * 128 + oc * 8);
+    dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
   }
   __syncthreads();
 #pragma unroll 1
@@ -344,8 +363,8 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const ActiveArgs
     const int g = r >> 6, c = (r & 63) * 2;
     float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-    for (int qtr = 0; qtr < kKeyParts; ++qtr) {
-      const float2 f = *reinterpret_cast<const float2*>(part + 2 * (qtr * npairs + r));
+    for (int pi = 0; pi < kParts; ++pi) {
+      const float2 f = *reinterpret_cast<const float2*>(part + pi * G * 128 + g * 128 + c);
       s0 += f.x;
       s1 += f.y;
     }
@@ -444,7 +463,17 @@ int launch_active(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4*
   if (grid.x == 0 || grid.y == 0) return BNA_OK;
   auto launch = [&](auto kern) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<grid, kDecodeThreads, smem, stream>>>(a);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kDecodeThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, a);
   };
   const bool bf = dtype == BNA_BF16;
   switch (a.G) {
