@@ -93,6 +93,10 @@ constexpr int kCompressThreads = 256;
 template <typename T>
 __global__ void __launch_bounds__(kCompressThreads) compress_kernel(const CompressArgs a) {
   __shared__ float red[kCompressThreads * 8];
+  // programmatic dependent launch: wait for the previous kernel of the stream, then let
+  // the next one start launching
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int j = blockIdx.x;
   const int b = blockIdx.y / a.H, h = blockIdx.y % a.H;
   const int64_t first = a.pos0 + (int64_t)j * a.block_size;
@@ -392,10 +396,19 @@ int launch_compress(const bna_tensor4* x, bna_tensor4* out, int dtype, int block
                  (int)x->size[3], block_size, pos0, valid_len, ring, slot0};
   dim3 grid(n_blocks, (unsigned)(x->size[0] * x->size[1]), x2 ? 2u : 1u);
   if (n_blocks == 0 || grid.y == 0) return BNA_OK;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kCompressThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
   if (dtype == BNA_BF16)
-    compress_kernel<__nv_bfloat16><<<grid, kCompressThreads, 0, stream>>>(a);
+    cudaLaunchKernelEx(&cfg, compress_kernel<__nv_bfloat16>, a);
   else
-    compress_kernel<__half><<<grid, kCompressThreads, 0, stream>>>(a);
+    cudaLaunchKernelEx(&cfg, compress_kernel<__half>, a);
   return check_cuda(cudaGetLastError(), "compress_kernel launch");
 }
 

@@ -103,6 +103,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ PrefillArgs a) {
   using namespace sm100;
+  // programmatic dependent launch: wait for the previous kernel of the stream (and its
+  // memory), then let the next one start launching
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int QT = a.QT, G = a.G, QS = a.QS;
@@ -667,7 +671,17 @@ int launch_prefill(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4
   const int grid = a.total_units < nsm ? a.total_units : nsm;
   auto launch = [&](auto kern) {
     set_smem_limit_once(reinterpret_cast<const void*>(kern), dev, (int)smem);
-    kern<<<grid, kThreads, smem, stream>>>(mq, mk, mv, a);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, a);
   };
 #define BNA_PREFILL_CASE(NRV)                                          \
   case NRV:                                                            \
