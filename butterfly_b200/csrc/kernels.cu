@@ -129,13 +129,13 @@ __global__ void __launch_bounds__(128) append_kernel(const AppendArgs a) {
 }
 
 // ------------------------------------------------------------------------------ active / decode
-// One CTA (256 threads, 8 warps) per (query index, b * Hkv) serves the G query heads of a
-// KV head.  Keys are spread over the warps for both products: warp w takes keys
-// w, w+8, ...; each lane holds 4 head_dim columns (8-byte coalesced row loads straight
-// from the cache, q of all G heads in registers), scores are warp-shuffle reduced, one
-// warp per head does the softmax (exp2 domain), and the 8 warps' partial outputs are
-// summed through shared memory.  Optionally the CTA first appends the new token to the
-// ring and closes one block into the summary pool (fused decode step).
+// One CTA (512 threads) per (query index, b * Hkv) serves the G query heads of a KV head.
+// One round trip of cp.async brings the raw window rows, the routed summary rows (when the
+// host routed them) and the G query rows into shared memory.  Scores: one thread per
+// (key, head) dot product; softmax: one warp per head (exp2 domain); weighted sum: one
+// thread per (key range, head, 8 columns), the key ranges' partial sums reduced through
+// shared memory.  Optionally the CTA also closes one block into the summary pool and
+// appends the new token to the ring (fused decode step).
 struct ActiveArgs {
   int B, Hq, Hkv, G, Tq, dh, window;
   float scale_log2;
