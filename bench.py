@@ -295,7 +295,7 @@ def run_decode(dev, seed, reps, warmup):
             cache.decode_step(q[i], kn[i], vn[i], lays[i])
         torch.cuda.synchronize()
         cache.offset, cache.summary_offset, cache.summary_count, cache.tail_size = counters
-        with torch.cuda.graph(graph, stream=s):
+        with torch.cuda.graph(graph, stream=s, capture_error_mode="thread_local"):
             for i in range(DEC_STEPS):
                 outs.append(cache.decode_step(q[i], kn[i], vn[i], lays[i]))
     torch.cuda.synchronize()
@@ -474,7 +474,7 @@ def main():
     # The timed step (8 layers x compressor + prefill) replays from a CUDA graph, so the
     # Python/ctypes cost of 16 library calls per step stays off the device timeline.
     graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
+    with torch.cuda.graph(graph, capture_error_mode="thread_local"):
         step()
     for _ in range(args.warmup):
         graph.replay()
