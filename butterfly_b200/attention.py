@@ -132,17 +132,31 @@ def butterfly_compressed_attention(
     BS, N = int(layout.block_size), int(layout.num_blocks)
     if N != -(-int(T) // BS):
         raise ValueError(f"layout has {N} blocks but T={T} needs {-(-int(T) // BS)}")
+    out, lse, _, _ = prefill_with_summaries(q, k, v, layout, int(local_window_tokens), scale, return_lse)
+    return (out, lse) if return_lse else out
+
+
+def prefill_with_summaries(q, k, v, layout, window: int, scale: Optional[float] = None, return_lse: bool = False,
+                           k_sum_out: Optional[torch.Tensor] = None, v_sum_out: Optional[torch.Tensor] = None):
+    """Compressor + prefill kernel; returns (out, lse or None, k_sum, v_sum).
+
+    The block means land in ``k_sum_out``/``v_sum_out`` [B,Hkv,N,dh] when given (for
+    instance a two-pool cache's summary slots, so that a prefill hands its closed blocks
+    to the cache without a copy).  Shapes are checked by the caller."""
+    batch, H_q, T, dh = q.shape
+    BS, N = int(layout.block_size), int(layout.num_blocks)
     route, _keep = route_for(layout, q.device)
     if tuple(k.shape) == tuple(v.shape):
-        ks, vs = block_mean_summaries_kv(k, v, seq_len=T, block_size=BS, num_blocks=N)
+        ks, vs = block_mean_summaries_kv(k, v, seq_len=T, block_size=BS, num_blocks=N, k_out=k_sum_out,
+                                         v_out=v_sum_out)
     else:
-        ks = block_mean_summaries(k, seq_len=T, block_size=BS, num_blocks=N)
-        vs = block_mean_summaries(v, seq_len=T, block_size=BS, num_blocks=N)
+        ks = block_mean_summaries(k, seq_len=T, block_size=BS, num_blocks=N, out=k_sum_out)
+        vs = block_mean_summaries(v, seq_len=T, block_size=BS, num_blocks=N, out=v_sum_out)
     out = torch.empty((batch, T, H_q, dh), device=q.device, dtype=q.dtype).transpose(1, 2)
     lse = torch.empty((batch, H_q, T), device=q.device, dtype=torch.float32) if return_lse else None
     sc = float(scale) if scale is not None else 1.0 / math.sqrt(dh)
-    prefill_attention_into(q, k, v, ks, vs, out, lse, route, int(local_window_tokens), sc)
-    return (out, lse) if return_lse else out
+    prefill_attention_into(q, k, v, ks, vs, out, lse, route, int(window), sc)
+    return out, lse, ks, vs
 
 
 def prefill_attention_into(q, k, v, k_sum, v_sum, out, lse, route, window: int, scale: float, *,

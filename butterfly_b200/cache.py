@@ -124,6 +124,69 @@ class CompressedKVCache:
         self._trim(step)
         return closes
 
+    # ------------------------------------------------------------------ prefill hand-off
+    def reserve(self, batch: int, heads: int, head_dim: int, dtype: torch.dtype, device: torch.device) -> None:
+        """Allocate the pools now (normally done by the first append)."""
+        if self._tail_k is None:
+            self._allocate(int(batch), int(heads), int(head_dim), dtype, device)
+
+    def summary_slots(self, num_blocks: int):
+        """Views [B,H,num_blocks,dh] of the first summary slots, or None if the pool is
+        smaller.  A prefill can write its block means here directly: the closed blocks
+        become the cache's summaries and the slots past ``summary_count`` stay unused
+        until their block closes (which rewrites them)."""
+        if self._sum_k is None or int(num_blocks) > self.summary_capacity:
+            return None
+        return self._sum_k[:, :, : int(num_blocks)], self._sum_v[:, :, : int(num_blocks)]
+
+    def _advance_counters_chunked(self, total: int, step: int) -> None:
+        """Counter evolution of ``append`` over consecutive chunks of ``step`` tokens."""
+        if step <= 0:
+            raise ValueError("chunk_size must be positive")
+        for s in range(0, total, step):
+            n = min(step, total - s)
+            self._check_room(n)
+            self.tail_size += n
+            self.offset += n
+            closes = self._plan_closes()
+            self.summary_count += len(closes)
+            self.summary_offset += len(closes) * self.block_size
+            self._trim(n)
+
+    def adopt_prefill(self, keys: torch.Tensor, values: torch.Tensor, k_sum: torch.Tensor, v_sum: torch.Tensor,
+                      *, chunk_size: Optional[int] = None) -> None:
+        """Take over a one-shot prefill of T tokens as if it had been appended in chunks.
+
+        The counters become exactly those of ``append`` called on consecutive chunks of
+        ``chunk_size`` tokens (default ``max_chunk_size``; the reference harness feeds its
+        MLX cache ``kv_step`` chunks, bench_qwen_consumer_mlx.py:494-522), so the cache
+        keeps only its tail and the closed blocks' means instead of the whole prompt.
+        The closed summaries are the prefill's block means ``k_sum``/``v_sum``
+        [B,H,>=summary_count,dh] (the same fp32 means, summed in the same order, as a
+        close computes); they are copied unless they already are this cache's
+        ``summary_slots``.  Only the last ``tail_size`` rows of keys/values are copied
+        into the ring."""
+        _lib.require_cuda(keys, values, k_sum, v_sum)
+        if self.offset != 0:
+            raise RuntimeError("adopt_prefill needs an empty cache")
+        B, H, T, dh = keys.shape
+        if tuple(values.shape) != tuple(keys.shape):
+            raise ValueError("keys and values must have the same shape")
+        self.reserve(B, H, dh, keys.dtype, keys.device)
+        self._advance_counters_chunked(int(T), int(chunk_size) if chunk_size else self.max_chunk_size)
+        S = self.summary_count
+        if S > int(k_sum.shape[2]):
+            raise ValueError(f"prefill summaries hold {int(k_sum.shape[2])} blocks, the cache closed {S}")
+        if S and k_sum.data_ptr() != self._sum_k.data_ptr():
+            self._sum_k[:, :, :S].copy_(k_sum[:, :, :S])
+            self._sum_v[:, :, :S].copy_(v_sum[:, :, :S])
+        t0 = self.tail_start
+        if self.tail_size:
+            tk, tv, sk, sv = (_lib.t4(x) for x in (self._tail_k, self._tail_v, keys[:, :, t0:], values[:, :, t0:]))
+            _lib.check(_lib.lib().bna_cache_append(ctypes.byref(tk), ctypes.byref(tv), ctypes.byref(sk),
+                                                   ctypes.byref(sv), _lib.dtype_code(keys.dtype), t0, self.ring,
+                                                   _lib.stream_ptr(keys.device)))
+
     def update_and_fetch(self, keys: torch.Tensor, values: torch.Tensor):
         self.append(keys, values)
         return self.keys, self.values

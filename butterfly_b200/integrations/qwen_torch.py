@@ -285,6 +285,66 @@ def make_compressed_cache(model: nn.Module, base_cache: Any = None, *, max_kv_si
                                     max_kv_size=max_kv_size, max_chunk_size=max_chunk_size)
 
 
+class GraphedGreedyDecode:
+    """A fixed number of greedy decode steps of a swapped model, captured once in a CUDA graph.
+
+    Every swapped layer's decode step is one fused append + block-close + attention launch
+    with host-side cache counters, so a run of ``steps`` tokens from a given cache state is
+    a static sequence of launches: it is recorded once and replayed.  Construction runs the
+    steps once eagerly on the capture stream (library warm-up; ``eager_tokens`` keeps the
+    tokens it produced), puts the two-pool counters back, and captures the same steps.
+    ``replay()`` re-runs them from the post-prefill state: each replay rewrites the same
+    ring slots and summary slots with the same values, so replays are repeatable.  After
+    construction the cache counters stand at the end of the captured steps.
+
+    ``first_token`` [B,1] (device, int64) seeds step 0; ``tokens`` [B,steps] receives the
+    greedy tokens of each replay and ``logits`` [steps,B,vocab] their logits.
+    """
+
+    @torch.no_grad()
+    def __init__(self, model: nn.Module, cache: "CompressedButterflyCache", first_token: torch.Tensor, steps: int):
+        comp = cache.compressed
+        self.steps = int(steps)
+        self.input = first_token.detach().clone()
+        B = int(self.input.shape[0])
+        dev = self.input.device
+        self.tokens = torch.empty((B, self.steps), dtype=torch.int64, device=dev)
+        saved = {i: (c.offset, c.summary_offset, c.summary_count, c.tail_size) for i, c in comp.items()}
+        logits = []
+
+        def run():
+            logits.clear()
+            tok = self.input
+            for i in range(self.steps):
+                out = model(input_ids=tok, past_key_values=cache, use_cache=True)
+                lg = out.logits[:, -1]
+                tok = lg.argmax(-1, keepdim=True)
+                self.tokens[:, i:i + 1].copy_(tok)
+                logits.append(lg)
+
+        def restore():
+            for i, c in comp.items():
+                c.offset, c.summary_offset, c.summary_count, c.tail_size = saved[i]
+
+        stream = torch.cuda.Stream(device=dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(stream):
+            run()
+        torch.cuda.current_stream(dev).wait_stream(stream)
+        torch.cuda.synchronize(dev)
+        self.eager_tokens = self.tokens.clone()
+        self.eager_logits = torch.stack(logits).clone()
+        restore()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream, capture_error_mode="thread_local"):
+            run()
+            self.logits = torch.stack(logits)
+        torch.cuda.synchronize(dev)
+
+    def replay(self) -> None:
+        self.graph.replay()
+
+
 # ----------------------------------------------------------------------------- attention module
 class QwenCUDAButterflyAttention(nn.Module):
     """Wrap a stock Qwen3.5 full-attention layer with compressed Butterfly attention."""
@@ -378,9 +438,15 @@ class QwenCUDAButterflyAttention(nn.Module):
                 out = comp_cache.decode_step(q, k, v, lay, scale=scale)
                 backend = "compressed_cache_decode_step"
             elif cache_len == 0:
-                out = _attn.butterfly_compressed_attention(q, k, v, layout=lay, local_window_tokens=W, scale=scale)
-                comp_cache.append(k, v)
-                backend = "compressed_prefill+cache_append"
+                # The prefill's block means are written straight into the cache's summary
+                # slots; the cache then takes over the prompt as if fed in max_chunk_size
+                # chunks, keeping only its tail rows (no whole-prompt copy, no re-close).
+                comp_cache.reserve(k.shape[0], k.shape[1], k.shape[3], k.dtype, k.device)
+                slots = comp_cache.summary_slots(lay.num_blocks)
+                ks_out, vs_out = slots if slots is not None else (None, None)
+                out, _, ks, vs = _attn.prefill_with_summaries(q, k, v, lay, W, scale, False, ks_out, vs_out)
+                comp_cache.adopt_prefill(k, v, ks, vs)
+                backend = "compressed_prefill+cache_handoff"
             else:
                 comp_cache.append(k, v)
                 out = comp_cache.attend(q, lay, scale=scale)
@@ -463,7 +529,8 @@ def swap_qwen_attention_with_butterfly_cuda(model: nn.Module, cfg: Optional[Qwen
 swap_qwen_attention_with_wayfinder_cuda = swap_qwen_attention_with_butterfly_cuda
 
 __all__ = [
-    "QwenCUDAButterflyConfig", "QwenCUDAButterflyAttention", "CompressedButterflyCache", "compressed_config",
+    "QwenCUDAButterflyConfig", "QwenCUDAButterflyAttention", "CompressedButterflyCache", "GraphedGreedyDecode",
+    "compressed_config",
     "extract_qkv_from_qwen_attention", "iter_qwen_butterfly_layers", "make_compressed_cache",
     "restore_qwen_dense_attention", "swap_qwen_attention_with_butterfly_cuda",
 ]

@@ -187,6 +187,38 @@ def prefill_attention(q, k, v, neighbors, *, block_size: int, window: int,
     return out, lse
 
 
+def prefill_attention_blocks(q_blocks, k, v, neighbors, blocks, *, block_size: int, window: int,
+                             summary_round=None, scale: float | None = None):
+    """``prefill_attention`` evaluated only for the query blocks in ``blocks`` (sampled
+    rows of a long sequence).  ``q_blocks`` [B,Hq,len(blocks),BS,dh] holds those blocks'
+    query rows (rows past T zero); block means and selection are those of the whole
+    sequence given by k/v [B,Hkv,T,dh].  Returns (out fp32 [B,Hq,len(blocks),BS,dh],
+    lse fp32 [B,Hq,len(blocks),BS]); rows past T are meaningless."""
+    B, Hq, nsel, BS, dh = q_blocks.shape
+    Hkv, T = k.shape[1], k.shape[2]
+    G = Hq // Hkv
+    assert BS == block_size and nsel == len(blocks)
+    N = len(neighbors)
+    scale = 1.0 / math.sqrt(dh) if scale is None else scale
+    ks = block_means(k, BS, N)
+    vs = block_means(v, BS, N)
+    if summary_round is not None:
+        ks, vs = summary_round(ks), summary_round(vs)
+    raw_idx, raw_mask, summary_idx, summary_mask = prefill_index_tensors(neighbors, T, BS, window)
+    out = np.zeros((B, Hq, nsel, BS, dh), np.float32)
+    lse = np.zeros((B, Hq, nsel, BS), np.float32)
+    for i, b in enumerate(blocks):
+        kc = np.concatenate([k[:, :, raw_idx[b]].astype(np.float32), ks[:, :, summary_idx[b]]], axis=2)
+        vc = np.concatenate([v[:, :, raw_idx[b]].astype(np.float32), vs[:, :, summary_idx[b]]], axis=2)
+        mask = np.concatenate([raw_mask[b], summary_mask[b]], axis=1)                    # [BS,R+S]
+        qg = q_blocks[:, :, i].astype(np.float32).reshape(B, Hkv, G, BS, dh)
+        sc = np.einsum("bhgqd,bhkd->bhgqk", qg, kc).astype(np.float32) * scale
+        w, l = _softmax_rows(sc, mask[None, None, None])
+        out[:, :, i] = np.einsum("bhgqk,bhkd->bhgqd", w, vc).reshape(B, Hq, BS, dh)
+        lse[:, :, i] = l.reshape(B, Hq, BS)
+    return out, lse
+
+
 def active_attention(q, k, v, neighbors, query_positions, *, block_size: int, window: int,
                      summary_round=None, scale: float | None = None):
     """Active/decode rows over a full K/V history (:1125-1197).  Returns (out, lse)."""

@@ -69,3 +69,42 @@ def test_capacity_errors():
     with pytest.raises(RuntimeError):
         for _ in range(40):
             c.update(x[:, :, :1], x[:, :, :1])
+
+
+def test_sampled_block_prefill_equals_full_prefill():
+    """The sampled-row prefill oracle (used at 128k / 262k) equals the full oracle's rows."""
+    rng = np.random.default_rng(5)
+    B, Hq, Hkv, T, dh, BS, W = 1, 4, 2, 1000, 16, 64, 24
+    q = rng.standard_normal((B, Hq, T, dh), dtype=np.float32)
+    k = rng.standard_normal((B, Hkv, T, dh), dtype=np.float32)
+    v = rng.standard_normal((B, Hkv, T, dh), dtype=np.float32)
+    nb = _nb(T, BS, 3)
+    full, full_lse = oc.prefill_attention(q, k, v, nb, block_size=BS, window=W)
+    blocks = [0, 1, 5, 8, 15]
+    qb = np.zeros((B, Hq, len(blocks), BS, dh), np.float32)
+    for i, b in enumerate(blocks):
+        n = min(BS, T - b * BS)
+        qb[:, :, i, :n] = q[:, :, b * BS:b * BS + n]
+    got, got_lse = oc.prefill_attention_blocks(qb, k, v, nb, blocks, block_size=BS, window=W)
+    for i, b in enumerate(blocks):
+        n = min(BS, T - b * BS)
+        np.testing.assert_allclose(got[:, :, i, :n], full[:, :, b * BS:b * BS + n], atol=1e-5)
+        np.testing.assert_allclose(got_lse[:, :, i, :n], full_lse[:, :, b * BS:b * BS + n], atol=1e-5)
+
+
+def test_handoff_counters_equal_chunked_appends():
+    """A one-shot prefill handed to the cache ends with the counters of chunked appends
+    (the counter arithmetic alone; the device copy is checked in the GPU tests)."""
+    from butterfly_b200.cache import CompressedKVCache
+    for T, chunk, BS, W in [(10000, 1024, 128, 64), (131072, 4096, 128, 64), (777, 100, 16, 8), (64, 512, 128, 64)]:
+        ref = CompressedKVCacheRef(block_size=BS, local_window_tokens=W, max_chunk_size=chunk, max_kv_size=T + 64)
+        ref._allocate(1, 1, 1)
+        c = CompressedKVCache(block_size=BS, local_window_tokens=W, max_chunk_size=chunk, max_kv_size=T + 64)
+        c.tail_capacity = ref.tail_capacity
+        c.summary_capacity = ref.summary_capacity
+        for s in range(0, T, chunk):
+            n = min(chunk, T - s)
+            ref.update(np.zeros((1, 1, n, 1), np.float32), np.zeros((1, 1, n, 1), np.float32))
+        c._advance_counters_chunked(T, chunk)
+        assert (c.offset, c.summary_offset, c.summary_count, c.tail_start, c.tail_size) == tuple(
+            ref.counters()[x] for x in ("offset", "summary_offset", "summary_count", "tail_start", "tail_size"))

@@ -23,7 +23,11 @@ def _worker(rank, world, port, T, BS, W, layer, q_np, k_np, v_np, out_dir, drop_
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import datetime
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    # Spawned interpreters can take tens of seconds to import torch on a loaded host, so the
+    # rendezvous gets a generous limit; the dropped-rank case keeps a short one so that its
+    # collective fails quickly once the peer has gone.
+    limit = 20 if drop_rank >= 0 else 180
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=limit))
     from butterfly_b200.seqshard import ShardOps, sequence_sharded_prefill
     from oracle import topology as ot
     from oracle import torch_port
