@@ -24,10 +24,12 @@
 //
 // Warp roles (608 threads, one CTA per SM):
 //   warp 0        Q + K producer        warp 18        V producer
-//   warp 1        TMEM allocator + single-thread MMA issuer
-//   warps 2..17   two softmax/epilogue groups of 8 warps (units alternate between them);
-//                 two warps share each TMEM lane quarter and split the columns
-// TMEM (512 columns): group g's S/P tile at [128g, 128g+128), its O tile at 256 + 128g.
+//   warp 1        TMEM allocator + MMA issuer: the whole warp runs the issue code with
+//                 warp-uniform operands and one elected lane issues each tcgen05.mma
+//   warps 2..17   softmax/epilogue: all 16 warps work on every unit; the four warps of a
+//                 TMEM lane quarter split its columns in 8-column chunks, and while the
+//                 tensor pipe computes unit i's P.V they run unit i-1's epilogue
+// TMEM (512 columns): two S/P tiles at [0, 256) (unit parity) and two O tiles at [256, 512).
 #include <map>
 #include <mutex>
 #include <type_traits>
@@ -427,7 +429,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const volatile uint32_t* slot = unit_meta + (i & 7);
         uint32_t w = *slot;
         for (int spin = 0; (w >> 8) != (uint32_t)i && spin < (1 << 22); ++spin) w = *slot;
-        ns = (int)(w & 0xFFu);
+        if ((w >> 8) == (uint32_t)i) {
+          ns = (int)(w & 0xFFu);
+        } else {
+          // The producer never published this unit's count: record the failure (the host
+          // sees it through bna_take_device_error), wind the CTA down through the abort
+          // flag, and keep this unit's control flow uniform with no summary keys.
+          *abort_flag = 1;
+          atomicCAS(a.err, 0, 0x1000 | 9);
+        }
       }
       if (row == 0 && cq == 0) stamp(i, 5);
       tc_fence_after();

@@ -186,12 +186,14 @@ BNA_API int bna_decode_step(const bna_tensor4* q, const bna_tensor4* k_new, cons
 /* ---- Prefill without caller-provided scratch -------------------------------------------
  * No counterpart in the reference.  For callers that cannot allocate device memory
  * (no cudaMalloc inside their host framework's capture/allocator regions, or a fixed
- * memory plan): computes the K/V block means into an 8 MiB device array that the library
- * reserves at load time, then runs bna_prefill_attention over the whole sequence
- * (q_pos0 = kv_pos0 = 0, total_len = T).  Rejects problems whose block means exceed
- * 8 MiB (BNA_CAPACITY).  The array is shared by all calls: calls that overlap on the GPU
- * race.  The first call on a device resolves the array's address and should come
- * before any stream capture. */
+ * memory plan): computes the K/V block means into an 8 MiB device array, then runs
+ * bna_prefill_attention over the whole sequence (q_pos0 = kv_pos0 = 0, total_len = T).
+ * The array is reserved on each device when the library's device code loads there (the
+ * first call, under CUDA's default lazy loading), and that first call resolves its
+ * address: make it before any stream capture, and do not call this after a
+ * cudaDeviceReset of the device.  Rejects problems whose block means exceed 8 MiB
+ * (BNA_CAPACITY) and bad shapes before launching anything.  The array is shared by all
+ * calls: calls that overlap on the GPU race. */
 BNA_API int bna_prefill_attention_static_scratch(const bna_tensor4* q, const bna_tensor4* k,
                                                  const bna_tensor4* v, bna_tensor4* out, float* lse,
                                                  int64_t lse_stride_b, int64_t lse_stride_h, int32_t dtype,

@@ -3,7 +3,7 @@
 Hosts that embed this library inside another framework's graph-capture or allocator
 regions, or that run with a fixed device-memory plan, cannot cudaMalloc the two block-mean
 buffers the regular prefill path needs.  bna_prefill_attention_static_scratch keeps them
-in a device array reserved when the library loads.  This test calls it through the C ABI
+in a fixed device array of the library.  This test calls it through the C ABI
 twice in a row (different problems, so the second call starts from the first call's
 leftover scratch contents) and checks each result against the regular entry point, with
 the same tolerance as the other parity tests.  It lives in its own file, collected last.
@@ -23,11 +23,11 @@ pytestmark = pytest.mark.gpu
 TOL = 2e-2
 
 
-def _case(B, Hq, Hkv, T, layer, seed):
-    g = torch.Generator().manual_seed(seed)
-    q = torch.randn(B, Hq, T, 128, generator=g).bfloat16().cuda()
-    k = torch.randn(B, Hkv, T, 128, generator=g).bfloat16().cuda()
-    v = torch.randn(B, Hkv, T, 128, generator=g).bfloat16().cuda()
+def _case(B, Hq, Hkv, T, layer, seed, dtype=torch.bfloat16):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    q = torch.randn(B, Hq, T, 128, device="cuda", generator=g).to(dtype)
+    k = torch.randn(B, Hkv, T, 128, device="cuda", generator=g).to(dtype)
+    v = torch.randn(B, Hkv, T, 128, device="cuda", generator=g).to(dtype)
     lay = bb.build_block_butterfly_layout(seq_len=T, block_size=128, num_key_value_heads=Hkv,
                                           num_key_value_groups=Hq // Hkv, layer_idx=layer, local_window_blocks=1,
                                           sink_count=1, partner_count=1, partner_rule="causal_shift")
@@ -41,20 +41,29 @@ def _static_call(q, k, v, lay):
     tq, tk, tv, to = (_lib.t4(x) for x in (q, k, v, out))
     _lib.check(_lib.lib().bna_prefill_attention_static_scratch(
         ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv), ctypes.byref(to), lse.data_ptr(),
-        lse.stride(0), lse.stride(1), _lib.BF16, ctypes.byref(lay.route), 64, 1.0 / math.sqrt(dh),
+        lse.stride(0), lse.stride(1), _lib.dtype_code(q.dtype), ctypes.byref(lay.route), 64, 1.0 / math.sqrt(dh),
         _lib.stream_ptr(q.device)))
     return out, lse
 
 
+def _check(B, Hq, Hkv, T, layer, seed, dtype=torch.bfloat16):
+    q, k, v, lay = _case(B, Hq, Hkv, T, layer, seed, dtype)
+    got, got_lse = _static_call(q, k, v, lay)
+    ref, ref_lse = bb.butterfly_compressed_attention(q, k, v, layout=lay, local_window_tokens=64, return_lse=True)
+    torch.cuda.synchronize()
+    assert np.abs((got.float() - ref.float()).cpu().numpy()).max() <= TOL
+    assert np.abs((got_lse - ref_lse).cpu().numpy()).max() <= 1e-3
+
+
 def test_static_scratch_matches_regular_entry_point_twice():
     for (B, Hq, Hkv, T, layer, seed) in [(2, 8, 2, 5000, 3, 1), (1, 8, 2, 1300, 6, 2)]:
-        q, k, v, lay = _case(B, Hq, Hkv, T, layer, seed)
-        got, got_lse = _static_call(q, k, v, lay)
-        ref, ref_lse = bb.butterfly_compressed_attention(q, k, v, layout=lay, local_window_tokens=64,
-                                                         return_lse=True)
-        torch.cuda.synchronize()
-        assert np.abs((got.float() - ref.float()).cpu().numpy()).max() <= TOL
-        assert np.abs((got_lse - ref_lse).cpu().numpy()).max() <= 1e-3
+        _check(B, Hq, Hkv, T, layer, seed)
+
+
+def test_static_scratch_fp16_and_full_capacity():
+    _check(1, 8, 2, 3000, 4, 3, dtype=torch.float16)
+    # B * Hkv * num_blocks = 8 * 2 * 1024 = 16384: the V means end at the array's last byte
+    _check(8, 8, 2, 131072, 5, 4)
 
 
 def test_static_scratch_rejects_oversized_problem():
