@@ -257,6 +257,18 @@ class ModelBench:
 def run_model(args, ws, rank, local, dev, peaks):
     hbm_peak, _tc_burst, tc_sus, peak_kind = peaks
     mb = ModelBench(dev, rank)
+    # the swapped model with transformers' eager decoder-layer glue, for comparison
+    mb.prefill()
+    torch.cuda.synchronize()
+    e0, e1 = _events(2)
+    e0.record()
+    for _ in range(2):
+        mb.prefill()
+    e1.record()
+    torch.cuda.synchronize()
+    unfused_ms = _max_over_ranks(e0.elapsed_time(e1) / 2, ws)
+    from butterfly_b200.integrations.qwen_fused import fuse_qwen_decoder_layers
+    fuse_qwen_decoder_layers(mb.model)
     for _ in range(args.warmup):
         mb.prefill()
     torch.cuda.synchronize()
@@ -329,6 +341,9 @@ def run_model(args, ws, rank, local, dev, peaks):
     torch.cuda.empty_cache()
     return {
         "value": value, "ms": ms, "clocks": clocks,
+        "unfused": {"prefill_tok_per_s": round(MODEL_T * ws / (unfused_ms / 1000.0), 1), "ms_per_step": round(unfused_ms, 3),
+                    "what": "same model and attention kernels with transformers' eager decoder-layer glue "
+                            "(swap_qwen_attention_with_butterfly_cuda only, as the reference swaps)"},
         "e2e": {"value": round(MODEL_T * ws / (e2e_ms / 1000.0), 1), "unit": "tok/s",
                 "h2d_bytes_per_step": MODEL_T * 8, "d2h_bytes_per_step": MODEL["vocab"] * 2,
                 "path": "model(input_ids) from pinned host token ids (H2D inside the timed region), "
@@ -343,7 +358,7 @@ def run_model(args, ws, rank, local, dev, peaks):
                                      "the attention kernel below",
                      "attention_kernel": att},
         "decode": decode,
-        "launches_per_step": 3 * MODEL["layers"],
+        "launches_per_step": 8 * MODEL["layers"] + 1,
     }
 
 
@@ -1006,7 +1021,8 @@ def main():
         "data": "synthetic: random-init weights (seed 1), uniform random token ids (seeded per rank)",
         "config": {"workload": f"model-128k: 0.8B-class Qwen3.5 decoder, 24 layers, hidden 1024, Hq8/Hkv2, dh128, "
                                f"SwiGLU 3584, vocab 151936, every layer compressed Butterfly attention (BS128, W64, "
-                               f"causal_shift); prefill T={MODEL_T} into a fresh two-pool cache, logits_to_keep=1; "
+                               f"causal_shift) plus fused decoder-layer glue (fuse_qwen_decoder_layers); prefill "
+                               f"T={MODEL_T} into a fresh two-pool cache, logits_to_keep=1; "
                                f"then {MODEL_DECODE} greedy decode steps",
                    "global_batch": ws, "seq_len": MODEL_T, "parallelism": f"batch-sharded x{ws} (one sequence per GPU)",
                    "l2": "inputs larger than L2: 1.33 GB of weights and >=0.27 GB activations per layer pass"},
@@ -1014,11 +1030,13 @@ def main():
         "cpu_baseline": cpu,
         "e2e": m["e2e"],
         "gpu_launches": args.steps * m["launches_per_step"],
-        "gpu_launches_note": "our kernels per prefill: per layer the compressor, the prefill kernel and the "
-                             "cache hand-off append",
+        "gpu_launches_note": "our kernels per prefill: per layer input RMSNorm, q/k norm+RoPE, compressor, prefill "
+                             "kernel, cache hand-off append, sigmoid gate, residual+RMSNorm, SwiGLU (8), plus the "
+                             "final norm",
         "timing": "CUDA events around the timed prefills; decode from CUDA-graph replays",
         "clocks": m["clocks"],
         "decode": m["decode"],
+        "prefill_unfused_glue": m["unfused"],
         "layer": layer,
         "decode_batched": bdec,
     }

@@ -22,6 +22,7 @@ EXPORTED = (
     "bna_block_neighbors_host", "bna_prefill_selection_host", "bna_active_selection_host",
     "bna_prefill_selection_device", "bna_compress_blocks", "bna_compress_kv_blocks", "bna_prefill_attention",
     "bna_active_attention", "bna_cache_append", "bna_decode_step", "bna_prefill_attention_static_scratch",
+    "bna_rmsnorm", "bna_qk_norm_rope", "bna_gate_sigmoid_mul", "bna_swiglu",
 )
 
 
@@ -71,6 +72,11 @@ def lib() -> ctypes.CDLL:
             "bna_active_attention": (i32, [T4, T4, T4, T4, T4, T4, vp, i64, i64, i32, R, i32, vp, i64, i64, i64, i32, f32, vp]),
             "bna_cache_append": (i32, [T4, T4, T4, T4, i32, i64, i64, vp]),
             "bna_prefill_attention_static_scratch": (i32, [T4, T4, T4, T4, vp, i64, i64, i32, R, i32, f32, vp]),
+            "bna_rmsnorm": (i32, [vp, i64, vp, i64, vp, vp, i64, vp, i64, i64, i32, f32, i32, vp]),
+            "bna_qk_norm_rope": (i32, [vp, i64, i64, vp, i64, i64, vp, vp, vp, vp, i64, i32, vp, vp, i64, i32, i32, i32,
+                                       f32, i32, vp]),
+            "bna_gate_sigmoid_mul": (i32, [vp, vp, i64, i64, vp, i64, i32, i32, i32, vp]),
+            "bna_swiglu": (i32, [vp, i64, i64, vp, i64, i32, i32, vp]),
             "bna_decode_step": (i32, [T4, T4, T4, T4, T4, T4, T4, T4, vp, i64, i64, i32, R, i32, i64, i64, i64, i64, i32, f32, vp]),
         }
         for name, (res, args) in sig.items():

@@ -1,0 +1,348 @@
+// glue.cu — the decoder-layer steps on either side of the compressed attention path,
+// fused into single HBM-bound kernels.  Each one replaces a chain of eager elementwise
+// ops of the Qwen3.5 decoder layer that the reference runs around its attention
+// (bna/integrations/qwen_torch.py:535-573 before the attention, :1585-1591 after it; the
+// norms and MLP of transformers' Qwen3_5DecoderLayer around them):
+//   * rmsnorm:       [residual add +] Qwen3.5 RMSNorm  y = x * rsqrt(mean(x^2) + eps) * (1 + w)
+//   * qk_norm_rope:  per-head q/k RMSNorm + partial rotary embedding (rotate-half form)
+//   * gate_mul:      attention output * sigmoid(gate)
+//   * swiglu:        silu(gate) * up
+// Arithmetic follows the eager ops step by step: fp32 inside a norm, and after every
+// elementwise op of the 16-bit storage type the value is rounded to that type, as torch
+// does when it runs those ops one at a time on bf16 tensors.
+#include <cuda_runtime.h>
+
+#include <string>
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace bna {
+namespace {
+
+constexpr int kWarps = 8;  // warps per CTA of the row kernels
+
+template <typename T>
+__device__ __forceinline__ float round_to(float x) {
+  const uint32_t p = ElemTraits<T>::pack2(x, 0.f);
+  return ElemTraits<T>::unpack2(p).x;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float* f, bool bf) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 t = bf ? ElemTraits<__nv_bfloat16>::unpack2(w[e]) : ElemTraits<__half>::unpack2(w[e]);
+    f[2 * e] = t.x;
+    f[2 * e + 1] = t.y;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float* f) {
+  return make_uint4(ElemTraits<T>::pack2(f[0], f[1]), ElemTraits<T>::pack2(f[2], f[3]),
+                    ElemTraits<T>::pack2(f[4], f[5]), ElemTraits<T>::pack2(f[6], f[7]));
+}
+
+// ------------------------------------------------------------------------------ RMSNorm
+// One warp per row; lane l holds chunks l, l+32, ... of 8 elements (NC chunks per lane).
+struct NormArgs {
+  const uint8_t* x;
+  int64_t xs;
+  const uint8_t* res;
+  int64_t rs;
+  const uint8_t* w;
+  uint8_t* out;
+  int64_t os;
+  uint8_t* sum;
+  int64_t ss;
+  int64_t rows;
+  int hidden;
+  float eps;
+};
+
+template <typename T, int NC>
+__global__ void __launch_bounds__(kWarps * 32) rmsnorm_kernel(const NormArgs a) {
+  constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (row >= a.rows) return;
+  float v[NC * 8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    unpack8(ld_nc_128(a.x + 2 * (row * a.xs + col)), v + c * 8, bf);
+    if (a.res) {
+      float r[8];
+      unpack8(ld_nc_128(a.res + 2 * (row * a.rs + col)), r, bf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[c * 8 + e] = round_to<T>(v[c * 8 + e] + r[e]);
+      if (a.sum) st_128(a.sum + 2 * (row * a.ss + col), pack8<T>(v + c * 8));
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += v[c * 8 + e] * v[c * 8 + e];
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)a.hidden + a.eps);
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    float w[8];
+    unpack8(ld_nc_128(a.w + 2 * col), w, bf);
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = (v[c * 8 + e] * r) * (1.f + w[e]);
+    st_128(a.out + 2 * (row * a.os + col), pack8<T>(y));
+  }
+}
+
+// ------------------------------------------------------------------------------ q/k prep
+// One warp per (token, head) row of head_dim 128: lane l holds dims 4l..4l+3 (8 bytes).
+struct QKArgs {
+  const uint8_t* q;
+  int64_t q_tok, q_head;
+  const uint8_t* k;
+  int64_t k_tok, k_head;
+  const uint8_t* qw;
+  const uint8_t* kw;
+  const uint8_t* cos;
+  const uint8_t* sin;
+  int64_t cs_tok;
+  int rot;
+  uint8_t* q_out;
+  uint8_t* k_out;
+  int64_t tokens;
+  int Hq, Hkv;
+  float eps;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_kernel(const QKArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t item = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int H = a.Hq + a.Hkv;
+  if (item >= a.tokens * H) return;
+  const int64_t t = item / H;
+  const int h = (int)(item % H);
+  const bool isq = h < a.Hq;
+  const uint8_t* src = isq ? a.q + 2 * (t * a.q_tok + (int64_t)h * a.q_head)
+                           : a.k + 2 * (t * a.k_tok + (int64_t)(h - a.Hq) * a.k_head);
+  const uint8_t* wp = isq ? a.qw : a.kw;
+  uint8_t* dst = isq ? a.q_out + 2 * ((t * a.Hq + h) * 128) : a.k_out + 2 * ((t * a.Hkv + (h - a.Hq)) * 128);
+  const uint2 u = *reinterpret_cast<const uint2*>(src + 8 * lane);
+  const uint2 uw = *reinterpret_cast<const uint2*>(wp + 8 * lane);
+  float x[4], w[4];
+  {
+    const float2 a0 = ElemTraits<T>::unpack2(u.x), a1 = ElemTraits<T>::unpack2(u.y);
+    const float2 b0 = ElemTraits<T>::unpack2(uw.x), b1 = ElemTraits<T>::unpack2(uw.y);
+    x[0] = a0.x; x[1] = a0.y; x[2] = a1.x; x[3] = a1.y;
+    w[0] = b0.x; w[1] = b0.y; w[2] = b1.x; w[3] = b1.y;
+  }
+  const float ss = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
+  const float r = rsqrtf(ss * (1.f / 128.f) + a.eps);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) x[e] = round_to<T>((x[e] * r) * (1.f + w[e]));
+  // rotate-half partner of dim d (d < rot): d + rot/2 for the first half, d - rot/2 after
+  const int half_lanes = a.rot >> 3;  // lanes per half of the rotary dims
+  const bool in_rot = lane < 2 * half_lanes;
+  const bool first = lane < half_lanes;
+  const int src_lane = in_rot ? (first ? lane + half_lanes : lane - half_lanes) : lane;
+  float p[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) p[e] = __shfl_sync(0xffffffffu, x[e], src_lane);
+  if (in_rot) {
+    const uint2 uc = *reinterpret_cast<const uint2*>(a.cos + 2 * (t * a.cs_tok) + 8 * lane);
+    const uint2 us = *reinterpret_cast<const uint2*>(a.sin + 2 * (t * a.cs_tok) + 8 * lane);
+    const float2 c0 = ElemTraits<T>::unpack2(uc.x), c1 = ElemTraits<T>::unpack2(uc.y);
+    const float2 s0 = ElemTraits<T>::unpack2(us.x), s1 = ElemTraits<T>::unpack2(us.y);
+    const float c[4] = {c0.x, c0.y, c1.x, c1.y}, s[4] = {s0.x, s0.y, s1.x, s1.y};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float rh = first ? -p[e] : p[e];
+      x[e] = round_to<T>(round_to<T>(x[e] * c[e]) + round_to<T>(rh * s[e]));
+    }
+  }
+  *reinterpret_cast<uint2*>(dst + 8 * lane) = make_uint2(ElemTraits<T>::pack2(x[0], x[1]),
+                                                         ElemTraits<T>::pack2(x[2], x[3]));
+}
+
+// ------------------------------------------------------------------------------ gate, swiglu
+struct GateArgs {
+  const uint8_t* o;  // [tokens, heads, dh] contiguous
+  const uint8_t* g;  // token stride g_tok, head stride g_head
+  int64_t g_tok, g_head;
+  uint8_t* out;      // [tokens, heads * dh] contiguous
+  int64_t tokens;
+  int heads, dh;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) gate_mul_kernel(const GateArgs a) {
+  constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
+  const int per_row = a.heads * a.dh / 8;
+  const int per_head = a.dh / 8;
+  const int64_t n = a.tokens * per_row;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / per_row;
+    const int j = (int)(i % per_row);
+    const int h = j / per_head, c = j % per_head;
+    float o[8], g[8];
+    unpack8(ld_nc_128(a.o + 16 * i), o, bf);
+    unpack8(ld_nc_128(a.g + 2 * (t * a.g_tok + (int64_t)h * a.g_head + c * 8)), g, bf);
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = round_to<T>(o[e]) * round_to<T>(1.f / (1.f + expf(-g[e])));
+    st_128(a.out + 16 * i, pack8<T>(y));
+  }
+}
+
+struct SwigluArgs {
+  const uint8_t* gu;  // row r: gate at gu + r * stride, up at + up_off
+  int64_t stride, up_off;
+  uint8_t* out;       // [rows, inter] contiguous
+  int64_t rows;
+  int inter;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) swiglu_kernel(const SwigluArgs a) {
+  constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
+  const int per_row = a.inter / 8;
+  const int64_t n = a.rows * per_row;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / per_row;
+    const int c = (int)(i % per_row);
+    const uint8_t* base = a.gu + 2 * (r * a.stride + c * 8);
+    float g[8], u[8];
+    unpack8(ld_nc_128(base), g, bf);
+    unpack8(ld_nc_128(base + 2 * a.up_off), u, bf);
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = round_to<T>(g[e] / (1.f + expf(-g[e]))) * u[e];
+    st_128(a.out + 16 * i, pack8<T>(y));
+  }
+}
+
+int elementwise_grid(int64_t n) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (n + 255) / 256;
+  const int64_t cap = (int64_t)sms * 8;  // 8 resident 256-thread CTAs per SM
+  return (int)(want < cap ? (want > 0 ? want : 1) : cap);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+template <typename T>
+int launch_rmsnorm(const NormArgs& a, cudaStream_t s) {
+  const dim3 grid((unsigned)((a.rows + kWarps - 1) / kWarps)), block(kWarps * 32);
+  switch (a.hidden / 256) {
+    case 1: rmsnorm_kernel<T, 1><<<grid, block, 0, s>>>(a); break;
+    case 2: rmsnorm_kernel<T, 2><<<grid, block, 0, s>>>(a); break;
+    case 4: rmsnorm_kernel<T, 4><<<grid, block, 0, s>>>(a); break;
+    case 8: rmsnorm_kernel<T, 8><<<grid, block, 0, s>>>(a); break;
+    case 10: rmsnorm_kernel<T, 10><<<grid, block, 0, s>>>(a); break;
+    case 12: rmsnorm_kernel<T, 12><<<grid, block, 0, s>>>(a); break;
+    case 16: rmsnorm_kernel<T, 16><<<grid, block, 0, s>>>(a); break;
+    default: return fail(BNA_UNSUPPORTED, "rmsnorm: hidden must be 256 x {1,2,4,8,10,12,16}");
+  }
+  return check_cuda(cudaGetLastError(), "rmsnorm launch");
+}
+
+}  // namespace
+}  // namespace bna
+
+using namespace bna;
+
+extern "C" BNA_API int bna_rmsnorm(const void* x, int64_t x_stride, const void* res, int64_t res_stride,
+                                   const void* weight, void* out, int64_t out_stride, void* sum_out,
+                                   int64_t sum_stride, int64_t rows, int32_t hidden, float eps, int32_t dtype,
+                                   void* stream) {
+  if (rows < 0) return fail(BNA_BAD_SHAPE, "rmsnorm: rows must be >= 0");
+  if (rows == 0) return BNA_OK;
+  if (!x || !weight || !out) return fail(BNA_BAD_SHAPE, "rmsnorm: null pointer");
+  if (hidden <= 0 || hidden % 256) return fail(BNA_UNSUPPORTED, "rmsnorm: hidden must be a multiple of 256");
+  for (int64_t st : {x_stride, out_stride, res ? res_stride : (int64_t)8, sum_out ? sum_stride : (int64_t)8})
+    if (st % 8) return fail(BNA_BAD_STRIDE, "rmsnorm: row strides must be multiples of 8 elements");
+  for (const void* p : {x, weight, (const void*)out, res, (const void*)sum_out})
+    if (p && !aligned16(p)) return fail(BNA_BAD_STRIDE, "rmsnorm: pointers must be 16-byte aligned");
+  if (sum_out && !res) return fail(BNA_BAD_SHAPE, "rmsnorm: sum_out needs a residual input");
+  NormArgs a{static_cast<const uint8_t*>(x), x_stride, static_cast<const uint8_t*>(res), res_stride,
+             static_cast<const uint8_t*>(weight), static_cast<uint8_t*>(out), out_stride,
+             static_cast<uint8_t*>(sum_out), sum_stride, rows, hidden, eps};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == BNA_BF16) return launch_rmsnorm<__nv_bfloat16>(a, s);
+  if (dtype == BNA_F16) return launch_rmsnorm<__half>(a, s);
+  return fail(BNA_BAD_DTYPE, "rmsnorm: bfloat16 or float16 only");
+}
+
+extern "C" BNA_API int bna_qk_norm_rope(const void* q, int64_t q_tok_stride, int64_t q_head_stride, const void* k,
+                                        int64_t k_tok_stride, int64_t k_head_stride, const void* q_weight,
+                                        const void* k_weight, const void* cos, const void* sin,
+                                        int64_t cs_tok_stride, int32_t rot, void* q_out, void* k_out,
+                                        int64_t tokens, int32_t hq, int32_t hkv, int32_t head_dim, float eps,
+                                        int32_t dtype, void* stream) {
+  if (tokens < 0 || hq <= 0 || hkv < 0) return fail(BNA_BAD_SHAPE, "qk_norm_rope: bad sizes");
+  if (tokens == 0) return BNA_OK;
+  if (head_dim != 128) return fail(BNA_UNSUPPORTED, "qk_norm_rope: head_dim must be 128");
+  if (rot < 0 || rot > head_dim || rot % 8) return fail(BNA_UNSUPPORTED, "qk_norm_rope: rotary dims must be a multiple of 8 <= head_dim");
+  if (!q || !q_weight || !q_out || (hkv && (!k || !k_weight || !k_out)) || (rot && (!cos || !sin)))
+    return fail(BNA_BAD_SHAPE, "qk_norm_rope: null pointer");
+  for (int64_t st : {q_tok_stride, q_head_stride, k_tok_stride, k_head_stride, rot ? cs_tok_stride : (int64_t)4})
+    if (st % 4) return fail(BNA_BAD_STRIDE, "qk_norm_rope: strides must be multiples of 4 elements");
+  for (const void* p : {q, k, q_weight, k_weight, cos, sin, (const void*)q_out, (const void*)k_out})
+    if (p && (reinterpret_cast<uintptr_t>(p) & 7)) return fail(BNA_BAD_STRIDE, "qk_norm_rope: pointers must be 8-byte aligned");
+  QKArgs a{static_cast<const uint8_t*>(q), q_tok_stride, q_head_stride, static_cast<const uint8_t*>(k), k_tok_stride,
+           k_head_stride, static_cast<const uint8_t*>(q_weight), static_cast<const uint8_t*>(k_weight),
+           static_cast<const uint8_t*>(cos), static_cast<const uint8_t*>(sin), cs_tok_stride, rot,
+           static_cast<uint8_t*>(q_out), static_cast<uint8_t*>(k_out), tokens, hq, hkv, eps};
+  const int64_t items = tokens * (hq + hkv);
+  const dim3 grid((unsigned)((items + kWarps - 1) / kWarps)), block(kWarps * 32);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == BNA_BF16) qk_norm_rope_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(a);
+  else if (dtype == BNA_F16) qk_norm_rope_kernel<__half><<<grid, block, 0, s>>>(a);
+  else return fail(BNA_BAD_DTYPE, "qk_norm_rope: bfloat16 or float16 only");
+  return check_cuda(cudaGetLastError(), "qk_norm_rope launch");
+}
+
+extern "C" BNA_API int bna_gate_sigmoid_mul(const void* o, const void* gate, int64_t gate_tok_stride,
+                                            int64_t gate_head_stride, void* out, int64_t tokens, int32_t heads,
+                                            int32_t head_dim, int32_t dtype, void* stream) {
+  if (tokens < 0 || heads <= 0 || head_dim <= 0 || head_dim % 8) return fail(BNA_BAD_SHAPE, "gate_sigmoid_mul: bad sizes");
+  if (tokens == 0) return BNA_OK;
+  if (!o || !gate || !out) return fail(BNA_BAD_SHAPE, "gate_sigmoid_mul: null pointer");
+  if (gate_tok_stride % 8 || gate_head_stride % 8) return fail(BNA_BAD_STRIDE, "gate_sigmoid_mul: gate strides must be multiples of 8");
+  if (!aligned16(o) || !aligned16(gate) || !aligned16(out)) return fail(BNA_BAD_STRIDE, "gate_sigmoid_mul: pointers must be 16-byte aligned");
+  GateArgs a{static_cast<const uint8_t*>(o), static_cast<const uint8_t*>(gate), gate_tok_stride, gate_head_stride,
+             static_cast<uint8_t*>(out), tokens, heads, head_dim};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = elementwise_grid(tokens * heads * head_dim / 8);
+  if (dtype == BNA_BF16) gate_mul_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(a);
+  else if (dtype == BNA_F16) gate_mul_kernel<__half><<<grid, 256, 0, s>>>(a);
+  else return fail(BNA_BAD_DTYPE, "gate_sigmoid_mul: bfloat16 or float16 only");
+  return check_cuda(cudaGetLastError(), "gate_sigmoid_mul launch");
+}
+
+extern "C" BNA_API int bna_swiglu(const void* gate_up, int64_t row_stride, int64_t up_offset, void* out, int64_t rows,
+                                  int32_t inter, int32_t dtype, void* stream) {
+  if (rows < 0 || inter <= 0 || inter % 8) return fail(BNA_BAD_SHAPE, "swiglu: bad sizes");
+  if (rows == 0) return BNA_OK;
+  if (!gate_up || !out) return fail(BNA_BAD_SHAPE, "swiglu: null pointer");
+  if (row_stride % 8 || up_offset % 8) return fail(BNA_BAD_STRIDE, "swiglu: strides must be multiples of 8");
+  if (!aligned16(gate_up) || !aligned16(out)) return fail(BNA_BAD_STRIDE, "swiglu: pointers must be 16-byte aligned");
+  SwigluArgs a{static_cast<const uint8_t*>(gate_up), row_stride, up_offset, static_cast<uint8_t*>(out), rows, inter};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = elementwise_grid(rows * inter / 8);
+  if (dtype == BNA_BF16) swiglu_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(a);
+  else if (dtype == BNA_F16) swiglu_kernel<__half><<<grid, 256, 0, s>>>(a);
+  else return fail(BNA_BAD_DTYPE, "swiglu: bfloat16 or float16 only");
+  return check_cuda(cudaGetLastError(), "swiglu launch");
+}

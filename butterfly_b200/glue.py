@@ -1,0 +1,116 @@
+"""Fused decoder-layer steps around the compressed attention (through libbna_b200.so).
+
+Each function replaces a chain of eager ops of the Qwen3.5 decoder layer with one sm_100a
+kernel and keeps the eager arithmetic: fp32 inside a norm, each elementwise result rounded
+to the 16-bit storage type.
+
+  rmsnorm             Qwen3_5RMSNorm (x * rsqrt(mean(x^2) + eps) * (1 + w)), optionally
+                      after the residual add, returning the sum as well
+  qk_norm_rope        q_norm / k_norm + apply_rotary_pos_emb of extract_qkv_from_qwen_attention
+                      (reference bna/integrations/qwen_torch.py:535-573)
+  gate_sigmoid_mul    attn_output * sigmoid(gate) (reference qwen_torch.py:1585-1591)
+  swiglu              act_fn(gate_proj(x)) * up_proj(x) of Qwen3_5MLP, on a merged gate/up output
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+
+def _rows(x: torch.Tensor, hidden: int) -> tuple[int, int]:
+    """(rows, row stride) of a tensor whose last dim is contiguous and whose leading dims
+    flatten to evenly strided rows."""
+    if x.shape[-1] != hidden or x.stride(-1) != 1:
+        raise ValueError("last dimension must be contiguous and of the normalised size")
+    rows = x.numel() // hidden if hidden else 0
+    if x.dim() == 1:
+        return 1, hidden
+    st = x.stride(-2)
+    # leading dims must collapse onto the row stride
+    exp = st
+    for d in range(x.dim() - 2, -1, -1):
+        if x.shape[d] > 1 and x.stride(d) != exp:
+            raise ValueError("rows of the input must be evenly strided")
+        exp *= x.shape[d]
+    return rows, st
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: Optional[torch.Tensor] = None,
+            want_sum: bool = False):
+    """RMSNorm over the last dim; with ``residual`` the input is round(x + residual).
+    Returns y, or (y, x + residual) when ``want_sum``."""
+    _lib.require_cuda(x, weight)
+    H = int(x.shape[-1])
+    if weight.dtype != x.dtype or weight.numel() != H or not weight.is_contiguous():
+        raise ValueError("weight must be a contiguous [hidden] tensor of the input's dtype")
+    rows, xs = _rows(x, H)
+    out = torch.empty(x.shape, device=x.device, dtype=x.dtype)
+    rp, rs, sp, ss = None, 0, None, 0
+    s = None
+    if residual is not None:
+        if residual.shape != x.shape or residual.dtype != x.dtype:
+            raise ValueError("residual must match x")
+        _, rs = _rows(residual, H)
+        rp = residual.data_ptr()
+        if want_sum:
+            s = torch.empty(x.shape, device=x.device, dtype=x.dtype)
+            sp, ss = s.data_ptr(), H
+    _lib.check(_lib.lib().bna_rmsnorm(x.data_ptr(), xs, rp, rs, weight.data_ptr(), out.data_ptr(), H, sp, ss, rows,
+                                      H, float(eps), _lib.dtype_code(x.dtype), _lib.stream_ptr(x.device)))
+    return (out, s) if want_sum else out
+
+
+def qk_norm_rope(q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor,
+                 cos: torch.Tensor, sin: torch.Tensor, eps: float):
+    """q [B,T,Hq,128], k [B,T,Hkv,128] (token-major, any token/head strides, dim
+    contiguous; q may be the query half of a gated q_proj output) -> normalised, rotated
+    q and k as contiguous [B,T,H,128].  cos/sin [B,T,rot] (rot = rotary dims)."""
+    _lib.require_cuda(q, k, q_weight, k_weight, cos, sin)
+    B, T, Hq, dh = q.shape
+    Hkv = int(k.shape[2])
+    rot = int(cos.shape[-1])
+    if q.stride(-1) != 1 or k.stride(-1) != 1:
+        raise ValueError("head_dim must be contiguous")
+    if B > 1 and (q.stride(0) != T * q.stride(1) or k.stride(0) != T * k.stride(1)):
+        raise ValueError("batch and token dims of q/k must flatten to one token stride")
+    cs = cos.reshape(B * T, rot) if cos.shape[0] == B else cos.expand(B, T, rot).reshape(B * T, rot)
+    sn = sin.reshape(B * T, rot) if sin.shape[0] == B else sin.expand(B, T, rot).reshape(B * T, rot)
+    cs, sn = cs.contiguous(), sn.contiguous()
+    for w in (q_weight, k_weight):
+        if w.dtype != q.dtype or w.numel() != dh or not w.is_contiguous():
+            raise ValueError("norm weights must be contiguous [head_dim] tensors of q's dtype")
+    qo = torch.empty((B, T, Hq, dh), device=q.device, dtype=q.dtype)
+    ko = torch.empty((B, T, Hkv, dh), device=q.device, dtype=q.dtype)
+    _lib.check(_lib.lib().bna_qk_norm_rope(
+        q.data_ptr(), q.stride(1), q.stride(2), k.data_ptr(), k.stride(1), k.stride(2), q_weight.data_ptr(),
+        k_weight.data_ptr(), cs.data_ptr(), sn.data_ptr(), rot, rot, qo.data_ptr(), ko.data_ptr(), B * T, Hq, Hkv,
+        dh, float(eps), _lib.dtype_code(q.dtype), _lib.stream_ptr(q.device)))
+    return qo, ko
+
+
+def gate_sigmoid_mul(o: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
+    """o [B,T,H,dh] contiguous, gate [B,T,H,dh] (dim contiguous) -> [B,T,H*dh]."""
+    _lib.require_cuda(o, gate)
+    B, T, H, dh = o.shape
+    if not o.is_contiguous():
+        raise ValueError("attention output must be contiguous [B,T,H,dh]")
+    if gate.stride(-1) != 1 or (B > 1 and gate.stride(0) != T * gate.stride(1)):
+        raise ValueError("gate rows must be evenly strided with a contiguous head_dim")
+    out = torch.empty((B, T, H * dh), device=o.device, dtype=o.dtype)
+    _lib.check(_lib.lib().bna_gate_sigmoid_mul(o.data_ptr(), gate.data_ptr(), gate.stride(1), gate.stride(2),
+                                               out.data_ptr(), B * T, H, dh, _lib.dtype_code(o.dtype),
+                                               _lib.stream_ptr(o.device)))
+    return out
+
+
+def swiglu(gate_up: torch.Tensor, inter: int) -> torch.Tensor:
+    """gate_up [..., 2*inter] (gate first, then up) -> silu(gate) * up [..., inter]."""
+    _lib.require_cuda(gate_up)
+    rows, st = _rows(gate_up, int(gate_up.shape[-1]))
+    out = torch.empty((*gate_up.shape[:-1], inter), device=gate_up.device, dtype=gate_up.dtype)
+    _lib.check(_lib.lib().bna_swiglu(gate_up.data_ptr(), st, inter, out.data_ptr(), rows, inter,
+                                     _lib.dtype_code(gate_up.dtype), _lib.stream_ptr(gate_up.device)))
+    return out

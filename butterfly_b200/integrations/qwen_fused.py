@@ -1,0 +1,157 @@
+"""Fused decoder-layer glue for Qwen3.5 layers already swapped onto compressed Butterfly.
+
+``swap_qwen_attention_with_butterfly_cuda`` replaces only the attention, as the reference
+does; the rest of each decoder layer still runs as transformers' eager ops, which at long
+prompts cost several times the GEMMs and the attention together (fp32 RMSNorm chains,
+rotary-embedding concatenations, separate sigmoid / SiLU / multiply / residual passes).
+``fuse_qwen_decoder_layers`` replaces that glue, per swapped layer, with:
+
+    h   = rmsnorm(x)                                  one kernel   (input_layernorm)
+    qkv = h @ [Wq; Wk; Wv]^T                          one GEMM     (q/k/v projections merged)
+    q,k = qk_norm_rope(q part, k part)                one kernel   (q_norm/k_norm + partial RoPE)
+    o   = compressed attention (prefill / decode)     the path's kernels
+    y   = o * sigmoid(gate)                           one kernel
+    a   = y @ Wo^T                                    one GEMM
+    x2, h2 = x + a, rmsnorm(x + a)                    one kernel   (residual + post_attention_layernorm)
+    gu  = h2 @ [Wg; Wu]^T                             one GEMM     (gate/up merged)
+    x2 += swiglu(gu) @ Wd^T                           one kernel + one GEMM accumulating into x2
+
+The projection weights are moved into one buffer per layer ([Wq; Wk; Wv] and [Wg; Wu]) and
+the modules' ``weight`` parameters become views of it, so the model's parameters, its
+``state_dict`` and the unfused path are unchanged.  Numerics follow the eager layer op by
+op except that the MLP's down projection is accumulated onto the residual in fp32 inside
+the GEMM (one rounding where the eager layer rounds twice).  A layer whose attention would
+fall back to dense attention (training, masks, ``output_attentions``) runs its original
+forward.  ``unfuse_qwen_decoder_layers`` restores the original forwards.
+"""
+from __future__ import annotations
+
+import time
+import types
+from typing import Any, Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .. import glue
+from .qwen_torch import QwenCUDAButterflyAttention, _get_decoder_with_layers
+
+
+def _is_qwen35_norm(mod: nn.Module) -> bool:
+    return type(mod).__name__ in ("Qwen3_5RMSNorm", "Qwen3_5MoeRMSNorm") and hasattr(mod, "weight")
+
+
+def _merge_weights(mods: list[nn.Linear]) -> torch.Tensor:
+    """Move the weights of ``mods`` into one [sum(out), in] buffer; each module's weight
+    becomes a view (Parameter) of its rows.  Returns the buffer."""
+    ws = [m.weight for m in mods]
+    buf = torch.cat([w.detach() for w in ws], 0)
+    r = 0
+    for m, w in zip(mods, ws):
+        n = w.shape[0]
+        m.weight = nn.Parameter(buf[r:r + n], requires_grad=w.requires_grad)
+        r += n
+    return buf
+
+
+class _FusedState:
+    def __init__(self, layer: nn.Module):
+        attn: QwenCUDAButterflyAttention = layer.self_attn
+        src = attn.fallback
+        mlp = layer.mlp
+        for lin in (src.q_proj, src.k_proj, src.v_proj, src.o_proj, mlp.gate_proj, mlp.up_proj, mlp.down_proj):
+            if getattr(lin, "bias", None) is not None:
+                raise ValueError("fused glue needs bias-free projections")
+        self.attn = attn
+        self.w_qkv = _merge_weights([src.q_proj, src.k_proj, src.v_proj])
+        self.w_gu = _merge_weights([mlp.gate_proj, mlp.up_proj])
+        self.hq, self.hkv, self.dh = attn.num_heads, attn.num_key_value_heads, attn.head_dim
+        self.inter = mlp.gate_proj.out_features
+
+
+def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=None, attention_mask=None,
+                         position_ids=None, past_key_values=None, **kwargs: Any):
+    st: _FusedState = self._bna_fused
+    attn = st.attn
+    B, T, H = hidden_states.shape
+    reason, comp_cache, cache_len, k_len_after = attn.plan(
+        T, attention_mask, past_key_values, bool(kwargs.get("output_attentions", False)))
+    if reason is not None or self.training or hidden_states.dtype not in (torch.bfloat16, torch.float16):
+        return type(self).forward(self, hidden_states, position_embeddings=position_embeddings,
+                                  attention_mask=attention_mask, position_ids=position_ids,
+                                  past_key_values=past_key_values, **kwargs)
+    t0 = time.perf_counter()
+    src = attn.fallback
+    hq, hkv, dh = st.hq, st.hkv, st.dh
+    x = hidden_states
+    h = glue.rmsnorm(x, self.input_layernorm.weight, self.input_layernorm.eps)
+    qkv = F.linear(h, st.w_qkv)                                   # [B,T,2*hq*dh + 2*hkv*dh]
+    nq = 2 * hq * dh
+    qg = qkv[..., :nq].view(B, T, hq, 2 * dh)                     # per head: query, then gate
+    k_raw = qkv[..., nq:nq + hkv * dh].view(B, T, hkv, dh)
+    v = qkv[..., nq + hkv * dh:].view(B, T, hkv, dh)
+    cos, sin = position_embeddings
+    q, k = glue.qk_norm_rope(qg[..., :dh], k_raw, src.q_norm.weight, src.k_norm.weight, cos, sin, src.q_norm.eps)
+    qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+    if comp_cache is None and past_key_values is not None:
+        kt, vt = past_key_values.update(kt, vt, attn.layer_idx)
+    out, backend, hit = attn.attend(qt, kt, vt, comp_cache, cache_len, k_len_after, kwargs.get("cache_position"))
+    y = glue.gate_sigmoid_mul(out.transpose(1, 2), qg[..., dh:])  # out storage is [B,T,hq,dh]
+    a = F.linear(y, src.o_proj.weight)
+    x2, h2 = glue.rmsnorm(a, self.post_attention_layernorm.weight, self.post_attention_layernorm.eps,
+                          residual=x, want_sum=True)
+    gu = F.linear(h2, st.w_gu)
+    act = glue.swiglu(gu, st.inter)
+    x2.view(-1, H).addmm_(act.view(-1, st.inter), self.mlp.down_proj.weight.t())
+    attn._profile(T, k_len_after, backend, hit, t0, fused=True)
+    return x2
+
+
+def _fused_norm_forward(self, x: torch.Tensor):
+    if x.dtype not in (torch.bfloat16, torch.float16) or not x.is_cuda:
+        return type(self).forward(self, x)
+    return glue.rmsnorm(x, self.weight, self.eps)
+
+
+def fuse_qwen_decoder_layers(model: nn.Module) -> list[int]:
+    """Run every swapped decoder layer (and the final norm) through the fused glue kernels.
+    Call after ``swap_qwen_attention_with_butterfly_cuda``; returns the fused layer indices."""
+    decoder = _get_decoder_with_layers(model)
+    fused = []
+    for idx, layer in enumerate(decoder.layers):
+        attn = getattr(layer, "self_attn", None)
+        if not isinstance(attn, QwenCUDAButterflyAttention) or hasattr(layer, "_bna_fused"):
+            if hasattr(layer, "_bna_fused"):
+                fused.append(idx)
+            continue
+        if not (_is_qwen35_norm(layer.input_layernorm) and _is_qwen35_norm(layer.post_attention_layernorm)
+                and _is_qwen35_norm(attn.fallback.q_norm) and _is_qwen35_norm(attn.fallback.k_norm)):
+            continue
+        if getattr(getattr(layer.mlp, "act_fn", None), "__class__", type(None)).__name__ not in ("SiLU", "SiLUActivation"):
+            continue
+        layer._bna_fused = _FusedState(layer)
+        layer.forward = types.MethodType(_fused_layer_forward, layer)
+        fused.append(idx)
+    norm = getattr(decoder, "norm", None)
+    if fused and norm is not None and _is_qwen35_norm(norm) and "forward" not in norm.__dict__:
+        norm.forward = types.MethodType(_fused_norm_forward, norm)
+    return fused
+
+
+def unfuse_qwen_decoder_layers(model: nn.Module) -> list[int]:
+    """Put back the original forwards (the merged weight buffers stay; modules see views)."""
+    decoder = _get_decoder_with_layers(model)
+    out = []
+    for idx, layer in enumerate(decoder.layers):
+        if hasattr(layer, "_bna_fused"):
+            del layer._bna_fused
+            layer.__dict__.pop("forward", None)
+            out.append(idx)
+    norm = getattr(decoder, "norm", None)
+    if norm is not None:
+        norm.__dict__.pop("forward", None)
+    return out
+
+
+__all__ = ["fuse_qwen_decoder_layers", "unfuse_qwen_decoder_layers"]

@@ -403,33 +403,28 @@ class QwenCUDAButterflyAttention(nn.Module):
             return "attention_mask"
         return None
 
-    def forward(self, hidden_states: torch.Tensor, position_embeddings: tuple[torch.Tensor, torch.Tensor],
-                attention_mask: Optional[torch.Tensor] = None, past_key_values: Optional[Any] = None,
-                cache_position: Optional[torch.LongTensor] = None, **kwargs: Any):
-        q_len = int(hidden_states.shape[1])
+    def plan(self, q_len: int, attention_mask, past_key_values, output_attentions: bool = False):
+        """(fallback reason or None, this layer's two-pool cache or None, cached length,
+        key length after this call) — the routing decision of ``forward``."""
         comp_cache = None
         if isinstance(past_key_values, CompressedButterflyCache):
             comp_cache = past_key_values.compressed.get(int(self.layer_idx)) if self.layer_idx is not None else None
         cache_len = comp_cache.size() if comp_cache is not None else _cache_seq_len(past_key_values, self.layer_idx)
         k_len_after = q_len + cache_len
-        output_attentions = bool(kwargs.get("output_attentions", False))
         reason = self._fallback_reason(attention_mask=attention_mask, q_len=q_len, k_len_after=k_len_after,
                                        output_attentions=output_attentions, compressed_cache=comp_cache is not None)
-        if reason is not None:
-            if comp_cache is not None:
-                raise RuntimeError(f"compressed cache layer {self.layer_idx} cannot fall back to dense attention "
-                                   f"({reason}): its K/V history lives in the two-pool cache")
-            self.last_profile = {"mode": "fallback", "reason": reason, "layer_idx": self.layer_idx,
-                                 "seq_len": q_len, "kv_len": k_len_after, "path": self.cfg.path}
-            return self.fallback(hidden_states, position_embeddings=position_embeddings,
-                                 attention_mask=attention_mask, past_key_values=past_key_values,
-                                 cache_position=cache_position, **kwargs)
-        if self.head_dim != 128:
+        if reason is not None and comp_cache is not None:
+            raise RuntimeError(f"compressed cache layer {self.layer_idx} cannot fall back to dense attention "
+                               f"({reason}): its K/V history lives in the two-pool cache")
+        if reason is None and self.head_dim != 128:
             raise ValueError(f"compressed Butterfly kernels need head_dim 128, layer has {self.head_dim}")
-        t0 = time.perf_counter()
-        hf_cache = None if comp_cache is not None else past_key_values
-        q, k, v, gate = extract_qkv_from_qwen_attention(self.fallback, hidden_states, position_embeddings,
-                                                        past_key_values=hf_cache, cache_position=cache_position)
+        return reason, comp_cache, cache_len, k_len_after
+
+    def attend(self, q, k, v, comp_cache, cache_len: int, k_len_after: int, cache_position=None):
+        """Compressed attention of q [B,Hq,Tq,dh] over k/v [B,Hkv,Tk,dh] (HF-cache history
+        included, or the new tokens only when ``comp_cache`` holds the history).  Returns
+        ([B,Hq,Tq,dh] view of [B,Tq,Hq,dh] storage, backend name, layout-cache hit)."""
+        q_len = int(q.shape[2])
         W = int(self.cfg.compressed_local_window_tokens)
         scale = 1.0 / math.sqrt(self.head_dim)  # SDPA's default, as the reference (the module scaling is not passed)
         lay, hit = self._layout(k_len_after)
@@ -460,16 +455,38 @@ class QwenCUDAButterflyAttention(nn.Module):
         else:
             out = _attn.butterfly_compressed_attention(q, k, v, layout=lay, local_window_tokens=W, scale=scale)
             backend = "compressed_butterfly"
+        return out, backend, hit
+
+    def _profile(self, q_len, k_len_after, backend, hit, t0, fused=False):
+        self.last_profile = {
+            "mode": "butterfly", "reason": None, "layer_idx": self.layer_idx, "seq_len": q_len,
+            "kv_len": k_len_after, "path": self.cfg.path, "engine": "bna_b200", "strategy": self.cfg.strategy,
+            "graph_cache_hit": bool(hit), "block_sparse_backend": backend, "fused_glue": bool(fused),
+            "elapsed_ms": float((time.perf_counter() - t0) * 1000.0),
+        }
+
+    def forward(self, hidden_states: torch.Tensor, position_embeddings: tuple[torch.Tensor, torch.Tensor],
+                attention_mask: Optional[torch.Tensor] = None, past_key_values: Optional[Any] = None,
+                cache_position: Optional[torch.LongTensor] = None, **kwargs: Any):
+        q_len = int(hidden_states.shape[1])
+        reason, comp_cache, cache_len, k_len_after = self.plan(
+            q_len, attention_mask, past_key_values, bool(kwargs.get("output_attentions", False)))
+        if reason is not None:
+            self.last_profile = {"mode": "fallback", "reason": reason, "layer_idx": self.layer_idx,
+                                 "seq_len": q_len, "kv_len": k_len_after, "path": self.cfg.path}
+            return self.fallback(hidden_states, position_embeddings=position_embeddings,
+                                 attention_mask=attention_mask, past_key_values=past_key_values,
+                                 cache_position=cache_position, **kwargs)
+        t0 = time.perf_counter()
+        hf_cache = None if comp_cache is not None else past_key_values
+        q, k, v, gate = extract_qkv_from_qwen_attention(self.fallback, hidden_states, position_embeddings,
+                                                        past_key_values=hf_cache, cache_position=cache_position)
+        out, backend, hit = self.attend(q, k, v, comp_cache, cache_len, k_len_after, cache_position)
         input_shape = hidden_states.shape[:-1]
         attn_output = out.transpose(1, 2).reshape(*input_shape, -1)  # storage is already [B, T, Hq, dh]
         attn_output = attn_output * torch.sigmoid(gate)
         attn_output = self.fallback.o_proj(attn_output)
-        self.last_profile = {
-            "mode": "butterfly", "reason": None, "layer_idx": self.layer_idx, "seq_len": q_len,
-            "kv_len": k_len_after, "path": self.cfg.path, "engine": "bna_b200", "strategy": self.cfg.strategy,
-            "graph_cache_hit": bool(hit), "block_sparse_backend": backend,
-            "elapsed_ms": float((time.perf_counter() - t0) * 1000.0),
-        }
+        self._profile(q_len, k_len_after, backend, hit, t0)
         return attn_output, None
 
 

@@ -183,6 +183,44 @@ BNA_API int bna_decode_step(const bna_tensor4* q, const bna_tensor4* k_new, cons
                     int64_t close_block, int64_t close_slot, int32_t num_summary_limit, float scale,
                     void* stream);
 
+/* ---- Decoder-layer steps around the attention (Qwen3.5) ---------------------------------
+ * Fused forms of the eager ops the reference runs before and after its attention
+ * (bna/integrations/qwen_torch.py:535-573 extract_qkv_from_qwen_attention: q/k RMSNorm and
+ * partial rotary embedding; :1585-1591: output gate; and transformers' Qwen3_5DecoderLayer
+ * norms and SwiGLU MLP around them).  16-bit storage (dtype), fp32 arithmetic inside a
+ * norm, each elementwise result rounded to the storage type as the eager ops do.  Row
+ * strides are in elements. */
+
+/* y = x * rsqrt(mean(x^2) + eps) * (1 + weight) per row of `hidden` elements (Qwen3.5
+ * RMSNorm).  With `res` non-NULL the normalised row is round(x + res) (the decoder layer's
+ * residual add), and that sum is also written to `sum_out` when non-NULL.  hidden must be
+ * 256 x {1,2,4,8,10,12,16}; pointers 16-byte aligned; strides multiples of 8. */
+BNA_API int bna_rmsnorm(const void* x, int64_t x_stride, const void* res, int64_t res_stride, const void* weight,
+                        void* out, int64_t out_stride, void* sum_out, int64_t sum_stride, int64_t rows,
+                        int32_t hidden, float eps, int32_t dtype, void* stream);
+
+/* q/k preparation for `tokens` tokens: per (token, head) RMSNorm over head_dim (1 + w form,
+ * q_weight / k_weight [head_dim]), then the rotary embedding on the first `rot` dims in
+ * rotate-half form with cos/sin [tokens, rot] (row stride cs_tok_stride), the remaining dims
+ * passed through.  Source row (t, h) of q is at q + t*q_tok_stride + h*q_head_stride (so the
+ * query half of a gated q_proj output is read in place); outputs are contiguous
+ * [tokens, hq, head_dim] and [tokens, hkv, head_dim].  head_dim must be 128. */
+BNA_API int bna_qk_norm_rope(const void* q, int64_t q_tok_stride, int64_t q_head_stride, const void* k,
+                             int64_t k_tok_stride, int64_t k_head_stride, const void* q_weight, const void* k_weight,
+                             const void* cos, const void* sin, int64_t cs_tok_stride, int32_t rot, void* q_out,
+                             void* k_out, int64_t tokens, int32_t hq, int32_t hkv, int32_t head_dim, float eps,
+                             int32_t dtype, void* stream);
+
+/* out[t, h*head_dim + d] = o[t, h, d] * sigmoid(gate[t, h, d]); o contiguous
+ * [tokens, heads, head_dim], gate strided (the gate half of a gated q_proj output). */
+BNA_API int bna_gate_sigmoid_mul(const void* o, const void* gate, int64_t gate_tok_stride, int64_t gate_head_stride,
+                                 void* out, int64_t tokens, int32_t heads, int32_t head_dim, int32_t dtype,
+                                 void* stream);
+
+/* out[r, i] = silu(gate_up[r, i]) * gate_up[r, up_offset + i] for i < inter; out contiguous. */
+BNA_API int bna_swiglu(const void* gate_up, int64_t row_stride, int64_t up_offset, void* out, int64_t rows,
+                       int32_t inter, int32_t dtype, void* stream);
+
 /* ---- Prefill without caller-provided scratch -------------------------------------------
  * No counterpart in the reference.  For callers that cannot allocate device memory
  * (no cudaMalloc inside their host framework's capture/allocator regions, or a fixed

@@ -1,0 +1,156 @@
+"""Fused decoder-layer glue kernels against the eager ops they replace, and a fused model
+against the unfused swapped model.
+
+Each kernel keeps the eager arithmetic (fp32 inside a norm, each elementwise result
+rounded to bf16); the norms' fp32 sums run in a different order, so results may differ by
+one bf16 rounding step: the bar is max |a - b| <= 2^-7 * max(|b|, 1) per element (one bf16
+ulp) and at least 99% of elements bit-identical.  The fused model's logits must stay
+within 3e-2 of the unfused model's (relative to the largest logit), its greedy tokens equal.
+"""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from butterfly_b200 import glue
+
+pytestmark = pytest.mark.gpu
+
+
+def _close(a, b, frac=0.99):
+    a, b = a.float(), b.float()
+    tol = (2.0 ** -7) * torch.clamp(b.abs(), min=1.0)
+    assert bool(((a - b).abs() <= tol).all()), float((a - b).abs().max())
+    assert float((a == b).float().mean()) >= frac
+
+
+def _norm(dim, seed):
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5RMSNorm
+    m = Qwen3_5RMSNorm(dim, eps=1e-6).cuda()
+    with torch.no_grad():
+        m.weight.copy_(torch.randn(dim, generator=torch.Generator().manual_seed(seed)) * 0.1)
+    return m.to(torch.bfloat16)
+
+
+def test_rmsnorm_matches_qwen35_norm():
+    g = torch.Generator(device="cuda").manual_seed(1)
+    for H in (1024, 2560, 256):
+        m = _norm(H, H)
+        x = torch.randn(3, 777, H, device="cuda", generator=g).bfloat16()
+        r = torch.randn(3, 777, H, device="cuda", generator=g).bfloat16()
+        _close(glue.rmsnorm(x, m.weight, m.eps), m(x))
+        y, s = glue.rmsnorm(x, m.weight, m.eps, residual=r, want_sum=True)
+        assert torch.equal(s, r + x)
+        _close(y, m(r + x))
+    # strided rows (a slice of a wider buffer)
+    m = _norm(1024, 5)
+    big = torch.randn(100, 2048, device="cuda", generator=g).bfloat16()
+    _close(glue.rmsnorm(big[:, 512:1536], m.weight, m.eps), m(big[:, 512:1536]))
+
+
+def test_qk_norm_rope_matches_eager():
+    from transformers import Qwen3_5TextConfig
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5TextRotaryEmbedding, apply_rotary_pos_emb
+    cfg = Qwen3_5TextConfig(hidden_size=1024, num_attention_heads=8, num_key_value_heads=2, head_dim=128,
+                            num_hidden_layers=1, layer_types=["full_attention"])
+    rope = Qwen3_5TextRotaryEmbedding(cfg).cuda()
+    g = torch.Generator(device="cuda").manual_seed(2)
+    B, T, Hq, Hkv, dh = 2, 700, 8, 2, 128
+    qkv = torch.randn(B, T, 2 * Hq * dh + 2 * Hkv * dh, device="cuda", generator=g).bfloat16() * 3
+    qg = qkv[..., :2 * Hq * dh].view(B, T, Hq, 2 * dh)
+    k_raw = qkv[..., 2 * Hq * dh:2 * Hq * dh + Hkv * dh].view(B, T, Hkv, dh)
+    qn, kn = _norm(dh, 11), _norm(dh, 12)
+    pos = torch.arange(5000, 5000 + T, device="cuda").view(1, T).expand(B, T)
+    cos, sin = rope(qkv, pos)
+    q, k = glue.qk_norm_rope(qg[..., :dh], k_raw, qn.weight, kn.weight, cos, sin, qn.eps)
+    rq = qn(qg[..., :dh]).transpose(1, 2)
+    rk = kn(k_raw).transpose(1, 2)
+    rq, rk = apply_rotary_pos_emb(rq, rk, cos, sin)
+    _close(q.transpose(1, 2), rq)
+    _close(k.transpose(1, 2), rk)
+
+
+def test_gate_and_swiglu_match_eager():
+    g = torch.Generator(device="cuda").manual_seed(3)
+    B, T, H, dh = 2, 333, 8, 128
+    o = torch.randn(B, T, H, dh, device="cuda", generator=g).bfloat16()
+    qg = torch.randn(B, T, H, 2 * dh, device="cuda", generator=g).bfloat16() * 4
+    gate = qg[..., dh:]
+    ref = o.reshape(B, T, -1) * torch.sigmoid(gate.reshape(B, T, -1))
+    _close(glue.gate_sigmoid_mul(o, gate), ref)
+    gu = torch.randn(B, T, 2 * 3584, device="cuda", generator=g).bfloat16() * 3
+    _close(glue.swiglu(gu, 3584), F.silu(gu[..., :3584]) * gu[..., 3584:])
+
+
+def _model(seed=6, layers=3, hidden=512, vocab=1000):
+    from transformers import Qwen3_5TextConfig
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5ForCausalLM
+
+    from butterfly_b200.integrations import qwen_torch as qt
+    qt.patch_qwen35_full_attention_decode()
+    cfg = Qwen3_5TextConfig(hidden_size=hidden, num_attention_heads=8, num_key_value_heads=2, head_dim=128,
+                            num_hidden_layers=layers, layer_types=["full_attention"] * layers,
+                            intermediate_size=1536, vocab_size=vocab)
+    torch.manual_seed(seed)
+    m = Qwen3_5ForCausalLM(cfg).eval().to(torch.bfloat16).cuda()
+    with torch.no_grad():  # non-trivial norm weights
+        for n, p in m.named_parameters():
+            if "norm" in n:
+                p.copy_(torch.randn_like(p.float()).mul(0.1).to(p.dtype))
+    qt.swap_qwen_attention_with_butterfly_cuda(m, qt.compressed_config())
+    return m
+
+
+@torch.no_grad()
+def test_fused_model_matches_unfused_prefill_and_decode():
+    from transformers import DynamicCache
+
+    from butterfly_b200.integrations import qwen_torch as qt
+    from butterfly_b200.integrations.qwen_fused import fuse_qwen_decoder_layers, unfuse_qwen_decoder_layers
+    m = _model()
+    ids = torch.randint(0, 1000, (2, 1500), generator=torch.Generator().manual_seed(7)).cuda()
+
+    def run(cache_kind):
+        cache = (qt.make_compressed_cache(m, DynamicCache(config=m.config), max_kv_size=2048, max_chunk_size=512)
+                 if cache_kind == "compressed" else DynamicCache(config=m.config))
+        out = m(input_ids=ids, past_key_values=cache, use_cache=True)
+        logits = [out.logits[:, -64:].float()]
+        tok = out.logits[:, -1].argmax(-1, keepdim=True)
+        toks = []
+        for _ in range(8):
+            out = m(input_ids=tok, past_key_values=cache, use_cache=True)
+            logits.append(out.logits[:, -1:].float())
+            tok = out.logits[:, -1].argmax(-1, keepdim=True)
+            toks.append(tok.view(-1).tolist())
+        return torch.cat(logits, 1), toks
+
+    ref_c, tok_c = run("compressed")
+    ref_h, tok_h = run("hf")
+    assert fuse_qwen_decoder_layers(m) == [0, 1, 2]
+    got_c, gtok_c = run("compressed")
+    for layer in qt.iter_qwen_butterfly_layers(m):
+        assert layer.last_profile["fused_glue"] is True
+    got_h, gtok_h = run("hf")
+    for ref, got in ((ref_c, got_c), (ref_h, got_h)):
+        scale = float(ref.abs().max())
+        assert float((got - ref).abs().max()) / scale < 3e-2
+    assert gtok_c[:4] == tok_c[:4] and gtok_h[:4] == tok_h[:4]
+    unfuse_qwen_decoder_layers(m)
+    back, _ = run("compressed")
+    assert torch.equal(back, ref_c)
+
+
+@torch.no_grad()
+def test_fused_model_graphed_decode():
+    from transformers import DynamicCache
+
+    from butterfly_b200.integrations import qwen_torch as qt
+    from butterfly_b200.integrations.qwen_fused import fuse_qwen_decoder_layers
+    m = _model(seed=8)
+    fuse_qwen_decoder_layers(m)
+    ids = torch.randint(0, 1000, (1, 2000), generator=torch.Generator().manual_seed(9)).cuda()
+    cache = qt.make_compressed_cache(m, DynamicCache(config=m.config), max_kv_size=4096, max_chunk_size=1024)
+    out = m(input_ids=ids, past_key_values=cache, use_cache=True, logits_to_keep=1)
+    gd = qt.GraphedGreedyDecode(m, cache, out.logits[:, -1].argmax(-1, keepdim=True), 16)
+    gd.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(gd.tokens, gd.eager_tokens)
