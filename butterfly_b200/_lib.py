@@ -22,7 +22,8 @@ EXPORTED = (
     "bna_block_neighbors_host", "bna_prefill_selection_host", "bna_active_selection_host",
     "bna_prefill_selection_device", "bna_compress_blocks", "bna_compress_kv_blocks", "bna_prefill_attention",
     "bna_active_attention", "bna_cache_append", "bna_decode_step", "bna_prefill_attention_static_scratch",
-    "bna_rmsnorm", "bna_qk_norm_rope", "bna_gate_sigmoid_mul", "bna_swiglu",
+    "bna_rmsnorm", "bna_qk_norm_rope", "bna_gate_sigmoid_mul", "bna_swiglu", "bna_gemv_rmsnorm", "bna_gemv_gated",
+    "bna_gemv",
 )
 
 
@@ -77,6 +78,9 @@ def lib() -> ctypes.CDLL:
                                        f32, i32, vp]),
             "bna_gate_sigmoid_mul": (i32, [vp, vp, i64, i64, vp, i64, i32, i32, i32, vp]),
             "bna_swiglu": (i32, [vp, i64, i64, vp, i64, i32, i32, vp]),
+            "bna_gemv_rmsnorm": (i32, [vp, i64, vp, i64, vp, f32, vp, i64, vp, i64, i64, i32, vp, i64, i32, i32, vp]),
+            "bna_gemv_gated": (i32, [vp, vp, i64, i64, i32, vp, i64, i64, vp, i64, vp, i64, i32, i32, vp]),
+            "bna_gemv": (i32, [vp, i64, vp, i64, i64, vp, i64, vp, i64, i32, i32, vp]),
             "bna_decode_step": (i32, [T4, T4, T4, T4, T4, T4, T4, T4, vp, i64, i64, i32, R, i32, i64, i64, i64, i64, i32, f32, vp]),
         }
         for name, (res, args) in sig.items():

@@ -124,33 +124,13 @@ struct QKArgs {
 };
 
 template <typename T>
-__global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_kernel(const QKArgs a) {
-  const int lane = threadIdx.x & 31;
-  const int64_t item = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
-  const int H = a.Hq + a.Hkv;
-  if (item >= a.tokens * H) return;
-  const int64_t t = item / H;
-  const int h = (int)(item % H);
-  const bool isq = h < a.Hq;
-  const uint8_t* src = isq ? a.q + 2 * (t * a.q_tok + (int64_t)h * a.q_head)
-                           : a.k + 2 * (t * a.k_tok + (int64_t)(h - a.Hq) * a.k_head);
-  const uint8_t* wp = isq ? a.qw : a.kw;
-  uint8_t* dst = isq ? a.q_out + 2 * ((t * a.Hq + h) * 128) : a.k_out + 2 * ((t * a.Hkv + (h - a.Hq)) * 128);
-  const uint2 u = *reinterpret_cast<const uint2*>(src + 8 * lane);
-  const uint2 uw = *reinterpret_cast<const uint2*>(wp + 8 * lane);
-  float x[4], w[4];
-  {
-    const float2 a0 = ElemTraits<T>::unpack2(u.x), a1 = ElemTraits<T>::unpack2(u.y);
-    const float2 b0 = ElemTraits<T>::unpack2(uw.x), b1 = ElemTraits<T>::unpack2(uw.y);
-    x[0] = a0.x; x[1] = a0.y; x[2] = a1.x; x[3] = a1.y;
-    w[0] = b0.x; w[1] = b0.y; w[2] = b1.x; w[3] = b1.y;
-  }
+__device__ __forceinline__ void qk_row(float (&x)[4], const float (&w)[4], float eps, int lane, int half_lanes,
+                                       const float (&c)[4], const float (&s)[4]) {
   const float ss = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
-  const float r = rsqrtf(ss * (1.f / 128.f) + a.eps);
+  const float r = rsqrtf(ss * (1.f / 128.f) + eps);
 #pragma unroll
   for (int e = 0; e < 4; ++e) x[e] = round_to<T>((x[e] * r) * (1.f + w[e]));
   // rotate-half partner of dim d (d < rot): d + rot/2 for the first half, d - rot/2 after
-  const int half_lanes = a.rot >> 3;  // lanes per half of the rotary dims
   const bool in_rot = lane < 2 * half_lanes;
   const bool first = lane < half_lanes;
   const int src_lane = in_rot ? (first ? lane + half_lanes : lane - half_lanes) : lane;
@@ -158,19 +138,52 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_kernel(const QKArgs 
 #pragma unroll
   for (int e = 0; e < 4; ++e) p[e] = __shfl_sync(0xffffffffu, x[e], src_lane);
   if (in_rot) {
-    const uint2 uc = *reinterpret_cast<const uint2*>(a.cos + 2 * (t * a.cs_tok) + 8 * lane);
-    const uint2 us = *reinterpret_cast<const uint2*>(a.sin + 2 * (t * a.cs_tok) + 8 * lane);
-    const float2 c0 = ElemTraits<T>::unpack2(uc.x), c1 = ElemTraits<T>::unpack2(uc.y);
-    const float2 s0 = ElemTraits<T>::unpack2(us.x), s1 = ElemTraits<T>::unpack2(us.y);
-    const float c[4] = {c0.x, c0.y, c1.x, c1.y}, s[4] = {s0.x, s0.y, s1.x, s1.y};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float rh = first ? -p[e] : p[e];
       x[e] = round_to<T>(round_to<T>(x[e] * c[e]) + round_to<T>(rh * s[e]));
     }
   }
-  *reinterpret_cast<uint2*>(dst + 8 * lane) = make_uint2(ElemTraits<T>::pack2(x[0], x[1]),
-                                                         ElemTraits<T>::pack2(x[2], x[3]));
+}
+
+__device__ __forceinline__ void unpack4(const uint2& u, float (&f)[4], bool bf) {
+  const float2 a = bf ? ElemTraits<__nv_bfloat16>::unpack2(u.x) : ElemTraits<__half>::unpack2(u.x);
+  const float2 b = bf ? ElemTraits<__nv_bfloat16>::unpack2(u.y) : ElemTraits<__half>::unpack2(u.y);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+}
+
+// One warp per token: every head row of the token (lane l holds dims 4l..4l+3), all loads
+// of the token issued before any arithmetic.
+template <typename T, int HQ, int HKV>
+__global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_kernel(const QKArgs a) {
+  constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (t >= a.tokens) return;
+  uint2 raw[HQ + HKV];
+#pragma unroll
+  for (int h = 0; h < HQ; ++h) raw[h] = *reinterpret_cast<const uint2*>(a.q + 2 * (t * a.q_tok + (int64_t)h * a.q_head) + 8 * lane);
+#pragma unroll
+  for (int h = 0; h < HKV; ++h)
+    raw[HQ + h] = *reinterpret_cast<const uint2*>(a.k + 2 * (t * a.k_tok + (int64_t)h * a.k_head) + 8 * lane);
+  const int half_lanes = a.rot >> 3;  // lanes per half of the rotary dims
+  float c[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+  if (lane < 2 * half_lanes) {
+    unpack4(*reinterpret_cast<const uint2*>(a.cos + 2 * (t * a.cs_tok) + 8 * lane), c, bf);
+    unpack4(*reinterpret_cast<const uint2*>(a.sin + 2 * (t * a.cs_tok) + 8 * lane), sn, bf);
+  }
+  float wq[4], wk[4];
+  unpack4(*reinterpret_cast<const uint2*>(a.qw + 8 * lane), wq, bf);
+  if (HKV) unpack4(*reinterpret_cast<const uint2*>(a.kw + 8 * lane), wk, bf);
+#pragma unroll
+  for (int h = 0; h < HQ + HKV; ++h) {
+    float x[4];
+    unpack4(raw[h], x, bf);
+    qk_row<T>(x, h < HQ ? wq : wk, a.eps, lane, half_lanes, c, sn);
+    uint8_t* dst = h < HQ ? a.q_out + 2 * ((t * HQ + h) * 128) : a.k_out + 2 * ((t * HKV + (h - HQ)) * 128);
+    *reinterpret_cast<uint2*>(dst + 8 * lane) = make_uint2(ElemTraits<T>::pack2(x[0], x[1]),
+                                                           ElemTraits<T>::pack2(x[2], x[3]));
+  }
 }
 
 // ------------------------------------------------------------------------------ gate, swiglu
@@ -183,24 +196,25 @@ struct GateArgs {
   int heads, dh;
 };
 
+// Thread = one 8-element vector of one token row; the grid covers all vectors once
+// (32-bit index arithmetic: tokens * heads * dh / 8 < 2^31 is checked on the host).
 template <typename T>
 __global__ void __launch_bounds__(256) gate_mul_kernel(const GateArgs a) {
   constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
-  const int per_row = a.heads * a.dh / 8;
-  const int per_head = a.dh / 8;
-  const int64_t n = a.tokens * per_row;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = i / per_row;
-    const int j = (int)(i % per_row);
-    const int h = j / per_head, c = j % per_head;
-    float o[8], g[8];
-    unpack8(ld_nc_128(a.o + 16 * i), o, bf);
-    unpack8(ld_nc_128(a.g + 2 * (t * a.g_tok + (int64_t)h * a.g_head + c * 8)), g, bf);
-    float y[8];
+  const int per_head = a.dh >> 3;
+  const int per_row = a.heads * per_head;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int)a.tokens * per_row) return;
+  const int t = i / per_row;
+  const int j = i - t * per_row;
+  const int h = j / per_head, c = j - h * per_head;
+  float o[8], g[8];
+  unpack8(ld_nc_128(a.o + 16 * (int64_t)i), o, bf);
+  unpack8(ld_nc_128(a.g + 2 * ((int64_t)t * a.g_tok + (int64_t)h * a.g_head + c * 8)), g, bf);
+  float y[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) y[e] = round_to<T>(o[e]) * round_to<T>(1.f / (1.f + expf(-g[e])));
-    st_128(a.out + 16 * i, pack8<T>(y));
-  }
+  for (int e = 0; e < 8; ++e) y[e] = o[e] * round_to<T>(1.f / (1.f + __expf(-g[e])));
+  st_128(a.out + 16 * (int64_t)i, pack8<T>(y));
 }
 
 struct SwigluArgs {
@@ -214,30 +228,22 @@ struct SwigluArgs {
 template <typename T>
 __global__ void __launch_bounds__(256) swiglu_kernel(const SwigluArgs a) {
   constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
-  const int per_row = a.inter / 8;
-  const int64_t n = a.rows * per_row;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / per_row;
-    const int c = (int)(i % per_row);
-    const uint8_t* base = a.gu + 2 * (r * a.stride + c * 8);
-    float g[8], u[8];
-    unpack8(ld_nc_128(base), g, bf);
-    unpack8(ld_nc_128(base + 2 * a.up_off), u, bf);
-    float y[8];
+  const int per_row = a.inter >> 3;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int)a.rows * per_row) return;
+  const int r = i / per_row;
+  const int c = i - r * per_row;
+  const uint8_t* base = a.gu + 2 * ((int64_t)r * a.stride + c * 8);
+  float g[8], u[8];
+  unpack8(ld_nc_128(base), g, bf);
+  unpack8(ld_nc_128(base + 2 * a.up_off), u, bf);
+  float y[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) y[e] = round_to<T>(g[e] / (1.f + expf(-g[e]))) * u[e];
-    st_128(a.out + 16 * i, pack8<T>(y));
-  }
+  for (int e = 0; e < 8; ++e) y[e] = round_to<T>(g[e] / (1.f + __expf(-g[e]))) * u[e];
+  st_128(a.out + 16 * (int64_t)i, pack8<T>(y));
 }
 
-int elementwise_grid(int64_t n) {
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t want = (n + 255) / 256;
-  const int64_t cap = (int64_t)sms * 8;  // 8 resident 256-thread CTAs per SM
-  return (int)(want < cap ? (want > 0 ? want : 1) : cap);
-}
+unsigned flat_grid(int64_t n) { return (unsigned)((n + 255) / 256); }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
@@ -304,13 +310,20 @@ extern "C" BNA_API int bna_qk_norm_rope(const void* q, int64_t q_tok_stride, int
            k_head_stride, static_cast<const uint8_t*>(q_weight), static_cast<const uint8_t*>(k_weight),
            static_cast<const uint8_t*>(cos), static_cast<const uint8_t*>(sin), cs_tok_stride, rot,
            static_cast<uint8_t*>(q_out), static_cast<uint8_t*>(k_out), tokens, hq, hkv, eps};
-  const int64_t items = tokens * (hq + hkv);
-  const dim3 grid((unsigned)((items + kWarps - 1) / kWarps)), block(kWarps * 32);
+  const dim3 grid((unsigned)((tokens + kWarps - 1) / kWarps)), block(kWarps * 32);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == BNA_BF16) qk_norm_rope_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(a);
-  else if (dtype == BNA_F16) qk_norm_rope_kernel<__half><<<grid, block, 0, s>>>(a);
-  else return fail(BNA_BAD_DTYPE, "qk_norm_rope: bfloat16 or float16 only");
-  return check_cuda(cudaGetLastError(), "qk_norm_rope launch");
+  if (dtype != BNA_BF16 && dtype != BNA_F16) return fail(BNA_BAD_DTYPE, "qk_norm_rope: bfloat16 or float16 only");
+  const bool bf = dtype == BNA_BF16;
+#define BNA_QK_CASE(HQ_, HKV_)                                                                   \
+  if (hq == HQ_ && hkv == HKV_) {                                                                 \
+    if (bf) qk_norm_rope_kernel<__nv_bfloat16, HQ_, HKV_><<<grid, block, 0, s>>>(a);             \
+    else qk_norm_rope_kernel<__half, HQ_, HKV_><<<grid, block, 0, s>>>(a);                       \
+    return check_cuda(cudaGetLastError(), "qk_norm_rope launch");                                 \
+  }
+  BNA_QK_CASE(8, 2) BNA_QK_CASE(16, 4) BNA_QK_CASE(8, 1) BNA_QK_CASE(8, 8) BNA_QK_CASE(4, 2) BNA_QK_CASE(16, 2)
+  BNA_QK_CASE(32, 8) BNA_QK_CASE(16, 8) BNA_QK_CASE(32, 4) BNA_QK_CASE(24, 4) BNA_QK_CASE(4, 1) BNA_QK_CASE(2, 1)
+#undef BNA_QK_CASE
+  return fail(BNA_UNSUPPORTED, "qk_norm_rope: unsupported (q heads, kv heads) pair");
 }
 
 extern "C" BNA_API int bna_gate_sigmoid_mul(const void* o, const void* gate, int64_t gate_tok_stride,
@@ -324,7 +337,8 @@ extern "C" BNA_API int bna_gate_sigmoid_mul(const void* o, const void* gate, int
   GateArgs a{static_cast<const uint8_t*>(o), static_cast<const uint8_t*>(gate), gate_tok_stride, gate_head_stride,
              static_cast<uint8_t*>(out), tokens, heads, head_dim};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int grid = elementwise_grid(tokens * heads * head_dim / 8);
+  if (tokens * heads * (int64_t)head_dim / 8 >= (int64_t)1 << 31) return fail(BNA_UNSUPPORTED, "gate_sigmoid_mul: too many elements");
+  const unsigned grid = flat_grid(tokens * heads * head_dim / 8);
   if (dtype == BNA_BF16) gate_mul_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(a);
   else if (dtype == BNA_F16) gate_mul_kernel<__half><<<grid, 256, 0, s>>>(a);
   else return fail(BNA_BAD_DTYPE, "gate_sigmoid_mul: bfloat16 or float16 only");
@@ -340,7 +354,8 @@ extern "C" BNA_API int bna_swiglu(const void* gate_up, int64_t row_stride, int64
   if (!aligned16(gate_up) || !aligned16(out)) return fail(BNA_BAD_STRIDE, "swiglu: pointers must be 16-byte aligned");
   SwigluArgs a{static_cast<const uint8_t*>(gate_up), row_stride, up_offset, static_cast<uint8_t*>(out), rows, inter};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int grid = elementwise_grid(rows * inter / 8);
+  if (rows * (int64_t)inter / 8 >= (int64_t)1 << 31) return fail(BNA_UNSUPPORTED, "swiglu: too many elements");
+  const unsigned grid = flat_grid(rows * inter / 8);
   if (dtype == BNA_BF16) swiglu_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(a);
   else if (dtype == BNA_F16) swiglu_kernel<__half><<<grid, 256, 0, s>>>(a);
   else return fail(BNA_BAD_DTYPE, "swiglu: bfloat16 or float16 only");

@@ -10,6 +10,12 @@ to the 16-bit storage type.
                       (reference bna/integrations/qwen_torch.py:535-573)
   gate_sigmoid_mul    attn_output * sigmoid(gate) (reference qwen_torch.py:1585-1591)
   swiglu              act_fn(gate_proj(x)) * up_proj(x) of Qwen3_5MLP, on a merged gate/up output
+
+Decode-time projections (1..8 tokens), each one HBM-bound weight stream with the step
+before it and after it fused in:
+  gemv_rmsnorm        W @ rmsnorm(x [+ res]), optionally followed by SwiGLU over [gate; up] rows
+  gemv_gated          [res +] W @ (o * sigmoid(gate))
+  gemv                [res +] W @ x
 """
 from __future__ import annotations
 
@@ -36,6 +42,16 @@ def _rows(x: torch.Tensor, hidden: int) -> tuple[int, int]:
             raise ValueError("rows of the input must be evenly strided")
         exp *= x.shape[d]
     return rows, st
+
+
+def _token_stride(x: torch.Tensor) -> int:
+    """Stride between consecutive tokens of a [B,T,H,dh] view whose batch and token dims
+    flatten to one evenly strided token index (a size-1 dim's stride does not matter)."""
+    B, T = int(x.shape[0]), int(x.shape[1])
+    ts = x.stride(1) if T > 1 else x.stride(0)
+    if B > 1 and T > 1 and x.stride(0) != T * ts:
+        raise ValueError("batch and token dims must flatten to one token stride")
+    return ts
 
 
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: Optional[torch.Tensor] = None,
@@ -74,8 +90,7 @@ def qk_norm_rope(q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_wei
     rot = int(cos.shape[-1])
     if q.stride(-1) != 1 or k.stride(-1) != 1:
         raise ValueError("head_dim must be contiguous")
-    if B > 1 and (q.stride(0) != T * q.stride(1) or k.stride(0) != T * k.stride(1)):
-        raise ValueError("batch and token dims of q/k must flatten to one token stride")
+    qts, kts = _token_stride(q), _token_stride(k)
     cs = cos.reshape(B * T, rot) if cos.shape[0] == B else cos.expand(B, T, rot).reshape(B * T, rot)
     sn = sin.reshape(B * T, rot) if sin.shape[0] == B else sin.expand(B, T, rot).reshape(B * T, rot)
     cs, sn = cs.contiguous(), sn.contiguous()
@@ -85,7 +100,7 @@ def qk_norm_rope(q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_wei
     qo = torch.empty((B, T, Hq, dh), device=q.device, dtype=q.dtype)
     ko = torch.empty((B, T, Hkv, dh), device=q.device, dtype=q.dtype)
     _lib.check(_lib.lib().bna_qk_norm_rope(
-        q.data_ptr(), q.stride(1), q.stride(2), k.data_ptr(), k.stride(1), k.stride(2), q_weight.data_ptr(),
+        q.data_ptr(), qts, q.stride(2), k.data_ptr(), kts, k.stride(2), q_weight.data_ptr(),
         k_weight.data_ptr(), cs.data_ptr(), sn.data_ptr(), rot, rot, qo.data_ptr(), ko.data_ptr(), B * T, Hq, Hkv,
         dh, float(eps), _lib.dtype_code(q.dtype), _lib.stream_ptr(q.device)))
     return qo, ko
@@ -97,10 +112,11 @@ def gate_sigmoid_mul(o: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
     B, T, H, dh = o.shape
     if not o.is_contiguous():
         raise ValueError("attention output must be contiguous [B,T,H,dh]")
-    if gate.stride(-1) != 1 or (B > 1 and gate.stride(0) != T * gate.stride(1)):
-        raise ValueError("gate rows must be evenly strided with a contiguous head_dim")
+    if gate.stride(-1) != 1:
+        raise ValueError("gate head_dim must be contiguous")
+    gts = _token_stride(gate)
     out = torch.empty((B, T, H * dh), device=o.device, dtype=o.dtype)
-    _lib.check(_lib.lib().bna_gate_sigmoid_mul(o.data_ptr(), gate.data_ptr(), gate.stride(1), gate.stride(2),
+    _lib.check(_lib.lib().bna_gate_sigmoid_mul(o.data_ptr(), gate.data_ptr(), gts, gate.stride(2),
                                                out.data_ptr(), B * T, H, dh, _lib.dtype_code(o.dtype),
                                                _lib.stream_ptr(o.device)))
     return out
@@ -113,4 +129,71 @@ def swiglu(gate_up: torch.Tensor, inter: int) -> torch.Tensor:
     out = torch.empty((*gate_up.shape[:-1], inter), device=gate_up.device, dtype=gate_up.dtype)
     _lib.check(_lib.lib().bna_swiglu(gate_up.data_ptr(), st, inter, out.data_ptr(), rows, inter,
                                      _lib.dtype_code(gate_up.dtype), _lib.stream_ptr(gate_up.device)))
+    return out
+
+
+def _mat(x: torch.Tensor, K: int) -> tuple[int, int]:
+    """(tokens, row stride) of a [M, K] matrix view with a contiguous last dim."""
+    if x.dim() != 2 or x.shape[1] != K or x.stride(1) != 1:
+        raise ValueError(f"expected a [tokens, {K}] matrix with a contiguous last dim, got {tuple(x.shape)}")
+    return int(x.shape[0]), int(x.stride(0)) if x.shape[0] > 1 else K
+
+
+def gemv_rmsnorm(x: torch.Tensor, norm_weight: torch.Tensor, eps: float, w: torch.Tensor, *,
+                 residual: Optional[torch.Tensor] = None, want_sum: bool = False, swiglu: bool = False):
+    """W @ rmsnorm(x [+ residual]) for x [M, K] (M <= 8).  With ``swiglu`` W holds the gate
+    rows then the up rows and the result is silu(gate) * up [M, N/2].  Returns y, or
+    (y, x + residual) when ``want_sum``."""
+    _lib.require_cuda(x, norm_weight, w)
+    N, K = int(w.shape[0]), int(w.shape[1])
+    M, xs = _mat(x, K)
+    if not w.is_contiguous() or w.dtype != x.dtype or norm_weight.dtype != x.dtype or norm_weight.numel() != K:
+        raise ValueError("weights must be contiguous and of x's dtype")
+    out = torch.empty((M, N // 2 if swiglu else N), device=x.device, dtype=x.dtype)
+    rp, rs, sp, ss, s = None, 0, None, 0, None
+    if residual is not None:
+        _, rs = _mat(residual, K)
+        rp = residual.data_ptr()
+        if want_sum:
+            s = torch.empty((M, K), device=x.device, dtype=x.dtype)
+            sp, ss = s.data_ptr(), K
+    _lib.check(_lib.lib().bna_gemv_rmsnorm(x.data_ptr(), xs, rp, rs, norm_weight.data_ptr(), float(eps), sp, ss,
+                                           w.data_ptr(), N, K, int(bool(swiglu)), out.data_ptr(), out.shape[1], M,
+                                           _lib.dtype_code(x.dtype), _lib.stream_ptr(x.device)))
+    return (out, s) if want_sum else out
+
+
+def gemv_gated(o: torch.Tensor, gate: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None):
+    """[residual +] W @ (o * sigmoid(gate)); o [M,H,dh] contiguous, gate [M,H,dh] (dim contiguous)."""
+    _lib.require_cuda(o, gate, w)
+    M, H, dh = o.shape
+    N, K = int(w.shape[0]), int(w.shape[1])
+    if K != H * dh or not o.is_contiguous() or gate.stride(-1) != 1 or not w.is_contiguous():
+        raise ValueError("gemv_gated: o must be contiguous [M, H, dh] with H*dh = in_features")
+    out = torch.empty((M, N), device=o.device, dtype=o.dtype)
+    rp, rs = None, 0
+    if residual is not None:
+        _, rs = _mat(residual, N)
+        rp = residual.data_ptr()
+    gts = gate.stride(0) if M > 1 else H * gate.stride(1)
+    _lib.check(_lib.lib().bna_gemv_gated(o.data_ptr(), gate.data_ptr(), gts, gate.stride(1), dh, w.data_ptr(), N, K,
+                                         rp, rs, out.data_ptr(), N, M, _lib.dtype_code(o.dtype),
+                                         _lib.stream_ptr(o.device)))
+    return out
+
+
+def gemv(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """[residual +] W @ x for x [M, K] (M <= 8)."""
+    _lib.require_cuda(x, w)
+    N, K = int(w.shape[0]), int(w.shape[1])
+    M, xs = _mat(x, K)
+    if not w.is_contiguous() or w.dtype != x.dtype:
+        raise ValueError("weight must be contiguous and of x's dtype")
+    out = torch.empty((M, N), device=x.device, dtype=x.dtype)
+    rp, rs = None, 0
+    if residual is not None:
+        _, rs = _mat(residual, N)
+        rp = residual.data_ptr()
+    _lib.check(_lib.lib().bna_gemv(x.data_ptr(), xs, w.data_ptr(), N, K, rp, rs, out.data_ptr(), N, M,
+                                   _lib.dtype_code(x.dtype), _lib.stream_ptr(x.device)))
     return out

@@ -16,6 +16,12 @@ rotary-embedding concatenations, separate sigmoid / SiLU / multiply / residual p
     gu  = h2 @ [Wg; Wu]^T                             one GEMM     (gate/up merged)
     x2 += swiglu(gu) @ Wd^T                           one kernel + one GEMM accumulating into x2
 
+For a decode step (one token per sequence, up to 8 sequences) the projections are instead
+weight-streaming GEMV kernels with the neighbouring steps fused in: rmsnorm+qkv,
+gate+o_proj+residual, rmsnorm+gate/up+SwiGLU, down_proj+residual (plus q/k norm+RoPE and
+the fused cache decode step): six launches per layer, each overlapping the previous one's
+tail through programmatic dependent launch.
+
 The projection weights are moved into one buffer per layer ([Wq; Wk; Wv] and [Wg; Wu]) and
 the modules' ``weight`` parameters become views of it, so the model's parameters, its
 ``state_dict`` and the unfused path are unchanged.  Numerics follow the eager layer op by
@@ -85,8 +91,13 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
     src = attn.fallback
     hq, hkv, dh = st.hq, st.hkv, st.dh
     x = hidden_states
-    h = glue.rmsnorm(x, self.input_layernorm.weight, self.input_layernorm.eps)
-    qkv = F.linear(h, st.w_qkv)                                   # [B,T,2*hq*dh + 2*hkv*dh]
+    decode = T == 1 and B <= 8 and H % 256 == 0 and st.inter % 256 == 0
+    if decode:  # weight-streaming projections with the norms, gate and residual adds fused in
+        qkv = glue.gemv_rmsnorm(x.view(B, H), self.input_layernorm.weight, self.input_layernorm.eps,
+                                st.w_qkv).view(B, 1, -1)
+    else:
+        h = glue.rmsnorm(x, self.input_layernorm.weight, self.input_layernorm.eps)
+        qkv = F.linear(h, st.w_qkv)                               # [B,T,2*hq*dh + 2*hkv*dh]
     nq = 2 * hq * dh
     qg = qkv[..., :nq].view(B, T, hq, 2 * dh)                     # per head: query, then gate
     k_raw = qkv[..., nq:nq + hkv * dh].view(B, T, hkv, dh)
@@ -97,6 +108,14 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
     if comp_cache is None and past_key_values is not None:
         kt, vt = past_key_values.update(kt, vt, attn.layer_idx)
     out, backend, hit = attn.attend(qt, kt, vt, comp_cache, cache_len, k_len_after, kwargs.get("cache_position"))
+    if decode:
+        x2 = glue.gemv_gated(out.transpose(1, 2).reshape(B, hq, dh), qg[:, 0, :, dh:], src.o_proj.weight,
+                             residual=x.view(B, H))
+        act = glue.gemv_rmsnorm(x2, self.post_attention_layernorm.weight, self.post_attention_layernorm.eps,
+                                st.w_gu, swiglu=True)
+        x3 = glue.gemv(act, self.mlp.down_proj.weight, residual=x2)
+        attn._profile(T, k_len_after, backend, hit, t0, fused=True)
+        return x3.view(B, 1, H)
     y = glue.gate_sigmoid_mul(out.transpose(1, 2), qg[..., dh:])  # out storage is [B,T,hq,dh]
     a = F.linear(y, src.o_proj.weight)
     x2, h2 = glue.rmsnorm(a, self.post_attention_layernorm.weight, self.post_attention_layernorm.eps,

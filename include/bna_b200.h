@@ -221,6 +221,32 @@ BNA_API int bna_gate_sigmoid_mul(const void* o, const void* gate, int64_t gate_t
 BNA_API int bna_swiglu(const void* gate_up, int64_t row_stride, int64_t up_offset, void* out, int64_t rows,
                        int32_t inter, int32_t dtype, void* stream);
 
+/* Decode-time projections for 1..8 tokens (y = W x per token, W [out_features,
+ * in_features] row-major, in_features a multiple of 256), with the layer step before the
+ * projection fused in front of it and the one after it fused behind it.  Replace the
+ * eager decode-step ops of the same decoder layer (q/k/v, o, gate/up and down
+ * projections with their norms, gate and residual adds). */
+
+/* y = W rmsnorm(x [+ res]) (Qwen3.5 RMSNorm with norm_weight; x + res rounded and written to
+ * sum_out when non-NULL).  With swiglu != 0 the rows are [gate; up] halves and
+ * out[i] = silu(gate_i) * up_i for i < out_features / 2. */
+BNA_API int bna_gemv_rmsnorm(const void* x, int64_t x_stride, const void* res, int64_t res_stride,
+                             const void* norm_weight, float eps, void* sum_out, int64_t sum_stride, const void* w,
+                             int64_t out_features, int64_t in_features, int32_t swiglu, void* out,
+                             int64_t out_stride, int32_t tokens, int32_t dtype, void* stream);
+
+/* y = [res +] W (o * sigmoid(gate)): o [tokens, in_features] contiguous, gate[m, h, d] at
+ * gate + m*gate_tok_stride + h*gate_head_stride + d (heads of head_dim columns). */
+BNA_API int bna_gemv_gated(const void* o, const void* gate, int64_t gate_tok_stride, int64_t gate_head_stride,
+                           int32_t head_dim, const void* w, int64_t out_features, int64_t in_features,
+                           const void* res, int64_t res_stride, void* out, int64_t out_stride, int32_t tokens,
+                           int32_t dtype, void* stream);
+
+/* y = [res +] W x. */
+BNA_API int bna_gemv(const void* x, int64_t x_stride, const void* w, int64_t out_features, int64_t in_features,
+                     const void* res, int64_t res_stride, void* out, int64_t out_stride, int32_t tokens,
+                     int32_t dtype, void* stream);
+
 /* ---- Prefill without caller-provided scratch -------------------------------------------
  * No counterpart in the reference.  For callers that cannot allocate device memory
  * (no cudaMalloc inside their host framework's capture/allocator regions, or a fixed
