@@ -118,7 +118,7 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
         return x3.view(B, 1, H)
     y = glue.gate_sigmoid_mul(out.transpose(1, 2), qg[..., dh:])  # out storage is [B,T,hq,dh]
     a = F.linear(y, src.o_proj.weight)
-    x2, h2 = glue.rmsnorm(a, self.post_attention_layernorm.weight, self.post_attention_layernorm.eps,
+    h2, x2 = glue.rmsnorm(a, self.post_attention_layernorm.weight, self.post_attention_layernorm.eps,
                           residual=x, want_sum=True)
     gu = F.linear(h2, st.w_gu)
     act = glue.swiglu(gu, st.inter)

@@ -16,9 +16,9 @@ from butterfly_b200 import glue
 pytestmark = pytest.mark.gpu
 
 
-def _close(a, b, frac=0.99):
+def _close(a, b, frac=0.99, ulps=1):
     a, b = a.float(), b.float()
-    tol = (2.0 ** -7) * torch.clamp(b.abs(), min=1.0)
+    tol = ulps * (2.0 ** -7) * torch.clamp(b.abs(), min=1.0)
     assert bool(((a - b).abs() <= tol).all()), float((a - b).abs().max())
     assert float((a == b).float().mean()) >= frac
 
@@ -177,8 +177,10 @@ def test_decode_gemv_kernels_match_eager():
         _close(glue.gemv_rmsnorm(x, norm.weight, norm.eps, Wgu, swiglu=True), F.silu(gu[:, :I]) * gu[:, I:], 0.9)
         act = torch.randn(M, I, device="cuda", generator=g).bfloat16()
         _close(glue.gemv(act, Wd), F.linear(act, Wd), 0.9)
-        _close(glue.gemv(act, Wd, residual=r), r + F.linear(act, Wd), 0.9)
+        # the residual sum rounds once more: a one-ulp difference in the product can become
+        # one ulp of the (larger) sum
+        _close(glue.gemv(act, Wd, residual=r), r + F.linear(act, Wd), 0.9, ulps=2)
         o = torch.randn(M, Hq, dh, device="cuda", generator=g).bfloat16()
         qg = torch.randn(M, Hq, 2 * dh, device="cuda", generator=g).bfloat16()
         ref = r + F.linear(o.reshape(M, -1) * torch.sigmoid(qg[..., dh:].reshape(M, -1)), Wo)
-        _close(glue.gemv_gated(o, qg[..., dh:], Wo, residual=r), ref, 0.9)
+        _close(glue.gemv_gated(o, qg[..., dh:], Wo, residual=r), ref, 0.9, ulps=2)
