@@ -970,11 +970,33 @@ def profile_case(kind: str):
         for _ in range(3):
             prefill_attention_into(q, k, v, ks, vs, out, None, r, W, 1 / math.sqrt(DH))
         torch.cuda.synchronize()
-    elif kind == "model-prefill":
+    elif kind == "model-decode":
+        # greedy decode tokens of the fused model after a 128k prefill, inside an NVTX range
+        # named "decode" (ncu --nvtx --nvtx-include decode/)
+        from butterfly_b200.integrations.qwen_fused import fuse_qwen_decoder_layers
         mb = ModelBench(dev, 0)
+        fuse_qwen_decoder_layers(mb.model)
+        with torch.no_grad():
+            logits, cache = mb.prefill()
+            tok = logits[:, -1].argmax(-1, keepdim=True)
+            for i in range(4):
+                if i == 2:
+                    torch.cuda.synchronize()
+                    torch.cuda.nvtx.range_push("decode")
+                out = mb.model(input_ids=tok, past_key_values=cache, use_cache=True)
+                tok = out.logits[:, -1].argmax(-1, keepdim=True)
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_pop()
+    elif kind == "model-prefill":
+        from butterfly_b200.integrations.qwen_fused import fuse_qwen_decoder_layers
+        mb = ModelBench(dev, 0)
+        fuse_qwen_decoder_layers(mb.model)
         mb.prefill()
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("prefill")
         mb.prefill()
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     else:
         run_decode(dev, 0, reps=1, warmup=1)
     torch.cuda.synchronize()
@@ -991,7 +1013,7 @@ def main():
     ap.add_argument("--no-layer", action="store_true", help="skip the 32k attention-layer leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the batched-decode leg")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--profile-case", choices=["prefill", "decode", "prefill-trace", "model-prefill"], default=None,
+    ap.add_argument("--profile-case", choices=["prefill", "decode", "prefill-trace", "model-prefill", "model-decode"], default=None,
                     help="small case for ncu: warm-up, then the launches to capture")
     args = ap.parse_args()
     if args.profile_case:

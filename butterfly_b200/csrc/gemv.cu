@@ -11,7 +11,8 @@
 //
 // Each prologue/epilogue does the eager ops' arithmetic, rounding to the storage type where
 // the eager layer rounds.  The projection is HBM-bound (every weight byte is read once per
-// call): each warp owns R output rows and streams them with 128-bit loads, lane l taking
+// call): each warp owns one output row (the gate/up pair for SWIGLU) and streams it with
+// 128-bit loads, lane l taking
 // columns [8(32c + l), +8) of chunk c.  All of a warp's weight loads are issued before
 // griddepcontrol.wait, so under programmatic dependent launch the weight stream of a
 // projection overlaps the tail of the kernel that produces its input; x_in is then built
@@ -136,7 +137,7 @@ __device__ __forceinline__ void build_input(const GemvArgs& a, uint8_t* xs, floa
   __syncthreads();
 }
 
-// R rows per warp (two rows of a SWIGLU pair when EPI == SWIGLU), NPRE chunks of 256
+// R rows per warp (the two rows of a SWIGLU pair when EPI == SWIGLU), NPRE chunks of 256
 // columns preloaded per row before the dependency wait; further chunks are streamed.
 template <typename T, int PRO, int EPI, int R, int NPRE>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs a) {
@@ -219,8 +220,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs a)
   for (int r = 0; r < R; ++r)
 #pragma unroll
     for (int m = 0; m < kMaxM; ++m)
+      if (m < a.M) {
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc[r][m] += __shfl_xor_sync(0xffffffffu, acc[r][m], o);
+        for (int o = 16; o > 0; o >>= 1) acc[r][m] += __shfl_xor_sync(0xffffffffu, acc[r][m], o);
+      }
   if (lane != 0) return;
   for (int m = 0; m < a.M; ++m) {
     if (EPI == EPI_SWIGLU) {
@@ -245,9 +248,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs a)
   }
 }
 
+// One output row per warp (the gate/up row pair for SWIGLU), so even the 1024-row
+// projections spread over 128 CTAs; all of a row's chunks are preloaded when they fit.
 template <typename T, int PRO, int EPI>
 int launch_gemv(const GemvArgs& a, cudaStream_t s) {
-  constexpr int R = EPI == EPI_SWIGLU ? 2 : 2;
+  constexpr int R = EPI == EPI_SWIGLU ? 2 : 1;
   const int per_cta = kGemvWarps * (EPI == EPI_SWIGLU ? 1 : R);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((a.n_out + per_cta - 1) / per_cta));
@@ -261,7 +266,9 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   cfg.numAttrs = 1;
   const int nch = (int)(a.K >> 8);
   cudaError_t e;
-  auto kern = nch <= 4 ? gemv_kernel<T, PRO, EPI, R, 4> : gemv_kernel<T, PRO, EPI, R, 8>;
+  constexpr int kBig = R == 1 ? 16 : 8;
+  auto kern = nch <= 4 ? gemv_kernel<T, PRO, EPI, R, 4>
+                       : (nch <= 8 ? gemv_kernel<T, PRO, EPI, R, 8> : gemv_kernel<T, PRO, EPI, R, kBig>);
   if (cfg.dynamicSmemBytes > 48 * 1024) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
     if (e != cudaSuccess) return check_cuda(e, "gemv smem attribute");

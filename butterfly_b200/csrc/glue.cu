@@ -186,6 +186,32 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_kernel(const QKArgs 
   }
 }
 
+// Few tokens (decode): one warp per (token, head) row instead, so the rows of one token are
+// normalised in parallel rather than one after another.
+template <typename T, int HQ, int HKV>
+__global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_row_kernel(const QKArgs a) {
+  constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
+  const int lane = threadIdx.x & 31;
+  const int item = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (item >= (int)a.tokens * (HQ + HKV)) return;
+  const int t = item / (HQ + HKV), h = item - t * (HQ + HKV);
+  const bool isq = h < HQ;
+  const uint8_t* src = isq ? a.q + 2 * ((int64_t)t * a.q_tok + (int64_t)h * a.q_head)
+                           : a.k + 2 * ((int64_t)t * a.k_tok + (int64_t)(h - HQ) * a.k_head);
+  float x[4], w[4];
+  unpack4(*reinterpret_cast<const uint2*>(src + 8 * lane), x, bf);
+  unpack4(*reinterpret_cast<const uint2*>((isq ? a.qw : a.kw) + 8 * lane), w, bf);
+  const int half_lanes = a.rot >> 3;
+  float c[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+  if (lane < 2 * half_lanes) {
+    unpack4(*reinterpret_cast<const uint2*>(a.cos + 2 * ((int64_t)t * a.cs_tok) + 8 * lane), c, bf);
+    unpack4(*reinterpret_cast<const uint2*>(a.sin + 2 * ((int64_t)t * a.cs_tok) + 8 * lane), sn, bf);
+  }
+  qk_row<T>(x, w, a.eps, lane, half_lanes, c, sn);
+  uint8_t* dst = isq ? a.q_out + 2 * (((int64_t)t * HQ + h) * 128) : a.k_out + 2 * (((int64_t)t * HKV + (h - HQ)) * 128);
+  *reinterpret_cast<uint2*>(dst + 8 * lane) = make_uint2(ElemTraits<T>::pack2(x[0], x[1]), ElemTraits<T>::pack2(x[2], x[3]));
+}
+
 // ------------------------------------------------------------------------------ gate, swiglu
 struct GateArgs {
   const uint8_t* o;  // [tokens, heads, dh] contiguous
@@ -314,11 +340,18 @@ extern "C" BNA_API int bna_qk_norm_rope(const void* q, int64_t q_tok_stride, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype != BNA_BF16 && dtype != BNA_F16) return fail(BNA_BAD_DTYPE, "qk_norm_rope: bfloat16 or float16 only");
   const bool bf = dtype == BNA_BF16;
-#define BNA_QK_CASE(HQ_, HKV_)                                                                   \
-  if (hq == HQ_ && hkv == HKV_) {                                                                 \
-    if (bf) qk_norm_rope_kernel<__nv_bfloat16, HQ_, HKV_><<<grid, block, 0, s>>>(a);             \
-    else qk_norm_rope_kernel<__half, HQ_, HKV_><<<grid, block, 0, s>>>(a);                       \
-    return check_cuda(cudaGetLastError(), "qk_norm_rope launch");                                 \
+  const bool per_row = tokens <= 64;
+  const dim3 grid_rows((unsigned)((tokens * (hq + hkv) + kWarps - 1) / kWarps));
+#define BNA_QK_CASE(HQ_, HKV_)                                                                      \
+  if (hq == HQ_ && hkv == HKV_) {                                                                    \
+    if (per_row) {                                                                                   \
+      if (bf) qk_norm_rope_row_kernel<__nv_bfloat16, HQ_, HKV_><<<grid_rows, block, 0, s>>>(a);     \
+      else qk_norm_rope_row_kernel<__half, HQ_, HKV_><<<grid_rows, block, 0, s>>>(a);               \
+    } else {                                                                                         \
+      if (bf) qk_norm_rope_kernel<__nv_bfloat16, HQ_, HKV_><<<grid, block, 0, s>>>(a);              \
+      else qk_norm_rope_kernel<__half, HQ_, HKV_><<<grid, block, 0, s>>>(a);                        \
+    }                                                                                                \
+    return check_cuda(cudaGetLastError(), "qk_norm_rope launch");                                    \
   }
   BNA_QK_CASE(8, 2) BNA_QK_CASE(16, 4) BNA_QK_CASE(8, 1) BNA_QK_CASE(8, 8) BNA_QK_CASE(4, 2) BNA_QK_CASE(16, 2)
   BNA_QK_CASE(32, 8) BNA_QK_CASE(16, 8) BNA_QK_CASE(32, 4) BNA_QK_CASE(24, 4) BNA_QK_CASE(4, 1) BNA_QK_CASE(2, 1)
