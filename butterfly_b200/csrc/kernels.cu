@@ -156,12 +156,18 @@ struct ActiveArgs {
   int host_ids[kMaxSummaries];
 };
 
-constexpr int kDecodeThreads = 512;
-constexpr int kDecodeWarps = kDecodeThreads / 32;
-constexpr int kKeyParts = kDecodeThreads / 64;  // P.V key ranges summed through shared memory
-// reduction buffer (floats): block-mean partials or the P.V partial sums
-__host__ __device__ constexpr int decode_red_floats(int G) {
-  return kDecodeThreads * 8 > kKeyParts * 128 * G ? kDecodeThreads * 8 : kKeyParts * 128 * G;
+// 512 threads (256 for G >= 8, where each warp keeps more per-head state in registers).
+__host__ __device__ constexpr int decode_threads(int G) { return G >= 8 ? 256 : 512; }
+// floats of the partial-sum region: the per-warp (o) partials, or the block-mean buffer of
+// a fused close (8 floats per thread)
+__host__ __device__ constexpr int decode_part_floats(int G) {
+  return (decode_threads(G) / 32) * G * 128 > decode_threads(G) * 8 ? (decode_threads(G) / 32) * G * 128
+                                                                     : decode_threads(G) * 8;
+}
+size_t decode_smem_bytes(int G, int window) {
+  const int maxk = window + kMaxSummaries;
+  return (size_t)2 * maxk * 256 + (size_t)G * 256 + sizeof(float) * (size_t)decode_part_floats(G) +
+         sizeof(float) * (size_t)(decode_threads(G) / 32) * G * 2 + sizeof(int) * (1 + kMaxSummaries);
 }
 
 __device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc) {
@@ -171,71 +177,99 @@ __device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// One CTA per (query index, b * Hkv) serves the G query heads of a KV head.
+//   1. loads: the raw window rows, the routed summary rows and the G query rows arrive in
+//      shared memory by cp.async in one round trip.  In a fused decode step the ring rows of
+//      positions <= p - 2 are requested before griddepcontrol.wait (under programmatic
+//      dependent launch, while the previous kernel of the stream finishes): only the
+//      immediately preceding kernel can still be running, and in a decode step the ring rows
+//      it may write are those of position p - 1 (the previous step's append) at most.
+//   2. one pass per warp: warp w takes keys w, w + NW, ...; for each key the G scores are
+//      warp all-reduced dot products (lane l holds dims 4l..4l+3) and an online softmax
+//      (exp2 domain) keeps each head's running max, sum and 128-wide output in registers.
+//   3. the NW per-warp (max, sum, output) partials of each head are merged once through
+//      shared memory (the online log-sum-exp merge) and written out.
+// Optionally the CTA also closes one block into the summary pool and appends the new token
+// to the ring (fused decode step).
 template <typename T, int G>
-__global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const ActiveArgs a) {
+__global__ void __launch_bounds__(decode_threads(G)) decode_kernel(const ActiveArgs a) {
+  constexpr int NT = decode_threads(G);
+  constexpr int NW = NT / 32;
   extern __shared__ __align__(16) uint8_t dsm_raw[];
   const int maxk = a.window + kMaxSummaries;
-  constexpr int kRow = 256 + 16;                                   // padded staged row (bank spread)
-  uint8_t* kv = dsm_raw;                                           // [2][maxk][kRow] K rows, V rows
-  uint8_t* qraw = kv + 2 * maxk * kRow;                            // [G][256 B] queries as loaded
-  float* sc = reinterpret_cast<float*>(qraw + G * 256);            // [G][maxk] scores -> weights
-  constexpr int kQRow = 132;  // scaled query row stride (floats): rows of different heads in different banks
-  float* qs = sc + G * maxk;                                       // [G][kQRow] scaled queries
-  float* red = qs + G * kQRow;                                     // block-mean / P.V reduction
-  constexpr int kRed = decode_red_floats(G);
-  float* stat = red + kRed;                                        // [G] row sums
-  int* sel = reinterpret_cast<int*>(stat + G);                     // [1 + 16] summary count + ids
+  uint8_t* kv = dsm_raw;                                      // [2][maxk][256 B] K rows, V rows
+  uint8_t* qraw = kv + 2 * maxk * 256;                        // [G][256 B] queries as loaded
+  float* part = reinterpret_cast<float*>(qraw + G * 256);     // [NW][G][128] partial outputs
+  float* red = part;                                          // block-mean buffer of a fused close
+  float* ml = part + decode_part_floats(G);                   // [NW][G][2] partial max, sum
+  int* sel = reinterpret_cast<int*>(ml + NW * G * 2);         // [1 + 16] summary count + ids
 
-  // Launched with programmatic stream serialization: this grid may start while the previous
-  // kernel of the stream finishes; wait for it (and its memory) before touching anything,
-  // then let the next step's grid start launching.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int t = blockIdx.x;
   const int b = blockIdx.y / a.Hkv, kvh = blockIdx.y % a.Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t p = a.positions ? a.positions[t] : a.pos0 + t;
+  const bool fused = a.knew != nullptr && a.ring > 0;
+  // positions come from the host in a fused step; a device positions array is an input
+  const int64_t p0 = a.positions ? -1 : a.pos0 + t;
 
-  // raw window [lo, hi]; with a fused append the newest row (p) is read from the input
-  int64_t lo = max64(0, p - a.window + 1);
-  if (a.ring == 0) lo = max64(lo, a.kv_pos0);
-  int64_t hi = p;
-  if (hi > a.kv_len - 1) hi = a.kv_len - 1;
-  const int nraw = hi >= lo ? (int)(hi - lo + 1) : 0;
-  const int ring = (int)a.ring;
-  const int idx_lo = ring > 0 ? (int)((uint64_t)lo % (uint64_t)a.ring) : (int)(lo - a.kv_pos0);
+  auto issue_rows = [&](int64_t lo, int idx_lo, int j0, int j1, int nraw) {
+    const int n = j1 - j0;
 #pragma unroll 1
-  for (int c = threadIdx.x; c < 2 * nraw * 16; c += kDecodeThreads) {
-    const int isv = c >= nraw * 16;
-    const int e = isv ? c - nraw * 16 : c;
-    const int j = e >> 4, ch = e & 15;
-    const uint8_t* src;
-    if (a.knew && j == nraw - 1) {
-      src = reinterpret_cast<const uint8_t*>(isv ? a.vnew : a.knew) +
-            2 * (b * (isv ? a.vn_b : a.kn_b) + kvh * (isv ? a.vn_h : a.kn_h));
-    } else {
-      int idx = idx_lo + j;
-      if (ring > 0 && idx >= ring) idx -= ring;
-      src = row_ptr(isv ? a.v : a.k, b, kvh, idx);
+    for (int c = threadIdx.x; c < 2 * n * 16; c += NT) {
+      const int isv = c >= n * 16;
+      const int e = isv ? c - n * 16 : c;
+      const int j = j0 + (e >> 4), ch = e & 15;
+      const uint8_t* src;
+      if (a.knew && j == nraw - 1) {
+        src = reinterpret_cast<const uint8_t*>(isv ? a.vnew : a.knew) +
+              2 * (b * (isv ? a.vn_b : a.kn_b) + kvh * (isv ? a.vn_h : a.kn_h));
+      } else {
+        int idx = idx_lo + j;
+        if (a.ring > 0 && idx >= (int)a.ring) idx -= (int)a.ring;
+        src = row_ptr(isv ? a.v : a.k, b, kvh, idx);
+      }
+      cp_async_16(kv + (isv * maxk + j) * 256 + ch * 16, src + ch * 16);
     }
-    cp_async_16(kv + (isv * maxk + j) * kRow + ch * 16, src + ch * 16);
+  };
+  // raw window [lo, hi]; with a fused append the newest row (p) is read from the input
+  auto window_of = [&](int64_t p, int64_t& lo, int& nraw, int& idx_lo) {
+    lo = max64(0, p - a.window + 1);
+    if (a.ring == 0) lo = max64(lo, a.kv_pos0);
+    int64_t hi = p;
+    if (hi > a.kv_len - 1) hi = a.kv_len - 1;
+    nraw = hi >= lo ? (int)(hi - lo + 1) : 0;
+    idx_lo = a.ring > 0 ? (int)((uint64_t)lo % (uint64_t)a.ring) : (int)(lo - a.kv_pos0);
+  };
+  int64_t lo = 0;
+  int nraw = 0, idx_lo = 0, npre = 0;
+  if (fused && p0 >= 0) {
+    window_of(p0, lo, nraw, idx_lo);
+    npre = (int)(p0 - 1 - lo);  // rows j < npre sit at positions <= p - 2
+    npre = npre < 0 ? 0 : (npre > nraw ? nraw : npre);
+    issue_rows(lo, idx_lo, 0, npre, nraw);
   }
+  // Launched with programmatic stream serialization: wait for the previous kernel of the
+  // stream (and its memory) before touching anything it may write, then let the next
+  // kernel start launching.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int64_t p = a.positions ? a.positions[t] : p0;
+  if (!(fused && p0 >= 0)) window_of(p, lo, nraw, idx_lo);
+  issue_rows(lo, idx_lo, npre, nraw, nraw);
   // host-routed summaries of a step that closes no block: their rows load together with
   // the window rows, in the same round trip (a block closed in this step is written below
   // and may be routed, so such steps load the summaries after the close)
   const bool early_sum = a.host_ns >= 0 && a.close_block < 0;
   if (early_sum) {
 #pragma unroll 1
-    for (int c = threadIdx.x; c < 2 * a.host_ns * 16; c += kDecodeThreads) {
+    for (int c = threadIdx.x; c < 2 * a.host_ns * 16; c += NT) {
       const int isv = c >= a.host_ns * 16;
       const int e = isv ? c - a.host_ns * 16 : c;
       const int j = e >> 4, ch = e & 15;
-      cp_async_16(kv + (isv * maxk + nraw + j) * kRow + ch * 16,
+      cp_async_16(kv + (isv * maxk + nraw + j) * 256 + ch * 16,
                   row_ptr(isv ? a.vs : a.ks, b, kvh, a.host_ids[j]) + ch * 16);
     }
   }
-  // queries: raw rows in the same round trip as the keys and values, scaled below
-  for (int c = threadIdx.x; c < G * 16; c += kDecodeThreads) {
+  for (int c = threadIdx.x; c < G * 16; c += NT) {
     const int g = c >> 4, ch = c & 15;
     cp_async_16(qraw + g * 256 + ch * 16, row_ptr(a.q, b, kvh * G + g, t) + ch * 16);
   }
@@ -258,12 +292,11 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const ActiveArgs
   const int ns = sel[0];
   const int nk = nraw + ns;
 #pragma unroll 1
-  for (int c = early_sum ? 2 * ns * 16 : threadIdx.x; c < 2 * ns * 16; c += kDecodeThreads) {
+  for (int c = early_sum ? 2 * ns * 16 : threadIdx.x; c < 2 * ns * 16; c += NT) {
     const int isv = c >= ns * 16;
     const int e = isv ? c - ns * 16 : c;
     const int j = e >> 4, ch = e & 15;
-    cp_async_16(kv + (isv * maxk + nraw + j) * kRow + ch * 16,
-                row_ptr(isv ? a.vs : a.ks, b, kvh, sel[1 + j]) + ch * 16);
+    cp_async_16(kv + (isv * maxk + nraw + j) * 256 + ch * 16, row_ptr(isv ? a.vs : a.ks, b, kvh, sel[1 + j]) + ch * 16);
   }
   cp_async_wait_all();
   __syncthreads();
@@ -274,107 +307,82 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const ActiveArgs
     const int isv = threadIdx.x >= 16;
     const int ch = threadIdx.x & 15;
     st_128(row_ptr(isv ? a.v : a.k, b, kvh, slot) + ch * 16,
-           *reinterpret_cast<const uint4*>(kv + (isv * maxk + nraw - 1) * kRow + ch * 16));
+           *reinterpret_cast<const uint4*>(kv + (isv * maxk + nraw - 1) * 256 + ch * 16));
   }
-#pragma unroll 1
-  for (int c = threadIdx.x; c < G * 64; c += kDecodeThreads) {  // queries, scaled to log2 units
-    const int g = c >> 6, d = (c & 63) * 2;
-    const float2 f = ElemTraits<T>::unpack2(*reinterpret_cast<const uint32_t*>(qraw + g * 256 + d * 2));
-    qs[g * kQRow + d] = f.x * a.scale_log2;
-    qs[g * kQRow + d + 1] = f.y * a.scale_log2;
-  }
-  __syncthreads();
 
-  // scores: one thread per (key, head), full 128-wide dot from shared memory
-#pragma unroll 1
-  for (int e = threadIdx.x; e < nk * G; e += kDecodeThreads) {
-    const int j = e / G, g = e - j * G;
-    const uint4* kr = reinterpret_cast<const uint4*>(kv + j * kRow);
-    const float4* q4 = reinterpret_cast<const float4*>(qs + g * kQRow);
-    float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
-#pragma unroll 4
-    for (int c = 0; c < 16; ++c) {
-      const uint4 u = kr[c];
-      const float4 qa = q4[2 * c], qb = q4[2 * c + 1];
-      const float2 f0 = ElemTraits<T>::unpack2(u.x), f1 = ElemTraits<T>::unpack2(u.y);
-      const float2 f2 = ElemTraits<T>::unpack2(u.z), f3 = ElemTraits<T>::unpack2(u.w);
-      d0 = fmaf(qa.x, f0.x, fmaf(qa.y, f0.y, d0));
-      d1 = fmaf(qa.z, f1.x, fmaf(qa.w, f1.y, d1));
-      d2 = fmaf(qb.x, f2.x, fmaf(qb.y, f2.y, d2));
-      d3 = fmaf(qb.z, f3.x, fmaf(qb.w, f3.y, d3));
-    }
-    sc[g * maxk + j] = (d0 + d1) + (d2 + d3);
+  // one pass per warp over its keys: scores, online softmax and weighted values
+  float qf[G][4];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const uint2 u = *reinterpret_cast<const uint2*>(qraw + g * 256 + 8 * lane);
+    const float2 f0 = ElemTraits<T>::unpack2(u.x), f1 = ElemTraits<T>::unpack2(u.y);
+    qf[g][0] = f0.x * a.scale_log2;
+    qf[g][1] = f0.y * a.scale_log2;
+    qf[g][2] = f1.x * a.scale_log2;
+    qf[g][3] = f1.y * a.scale_log2;
   }
-  __syncthreads();
-  // softmax: warp g (looping if G > warps) owns head g; weights overwrite the scores
+  float m[G], l[G], o[G][4];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+    o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+  }
 #pragma unroll 1
-  for (int g = warp; g < G; g += kDecodeWarps) {
-    float* sg = sc + g * maxk;
-    float m = -INFINITY;
-    for (int j = lane; j < nk; j += 32) m = fmaxf(m, sg[j]);
+  for (int j = warp; j < nk; j += NW) {
+    const uint2 uk = *reinterpret_cast<const uint2*>(kv + j * 256 + 8 * lane);
+    const uint2 uv = *reinterpret_cast<const uint2*>(kv + (maxk + j) * 256 + 8 * lane);
+    const float2 k0 = ElemTraits<T>::unpack2(uk.x), k1 = ElemTraits<T>::unpack2(uk.y);
+    const float2 v0 = ElemTraits<T>::unpack2(uv.x), v1 = ElemTraits<T>::unpack2(uv.y);
+    float s[G];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float l = 0.f;
-    for (int j = lane; j < nk; j += 32) {
-      const float e = exp2f(sg[j] - m);
-      sg[j] = e;
-      l += e;
+    for (int g = 0; g < G; ++g) s[g] = fmaf(qf[g][0], k0.x, fmaf(qf[g][1], k0.y, fmaf(qf[g][2], k1.x, qf[g][3] * k1.y)));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int g = 0; g < G; ++g) s[g] += __shfl_xor_sync(0xffffffffu, s[g], off);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float mn = fmaxf(m[g], s[g]);
+      const float c = exp2f(m[g] - mn);  // 0 on the first key (m = -inf)
+      const float pw = exp2f(s[g] - mn);
+      l[g] = fmaf(l[g], c, pw);
+      o[g][0] = fmaf(o[g][0], c, pw * v0.x);
+      o[g][1] = fmaf(o[g][1], c, pw * v0.y);
+      o[g][2] = fmaf(o[g][2], c, pw * v1.x);
+      o[g][3] = fmaf(o[g][3], c, pw * v1.y);
+      m[g] = mn;
     }
+  }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+  for (int g = 0; g < G; ++g) {
+    *reinterpret_cast<float4*>(part + (warp * G + g) * 128 + 4 * lane) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
     if (lane == 0) {
-      stat[g] = l;
-      if (a.lse) a.lse[b * a.ls_b + (int64_t)(kvh * G + g) * a.ls_h + t] = (m + log2f(l)) * 0.6931471805599453f;
+      ml[(warp * G + g) * 2] = m[g];
+      ml[(warp * G + g) * 2 + 1] = l[g];
     }
   }
   __syncthreads();
-  // weighted values: thread = (key range, head, 8 columns): one 16-byte V load and eight
-  // independent FMAs per key; the key ranges' partial sums meet in shared memory
-  // (reusing the block-mean buffer)
-  constexpr int kOct = G * 16;
-  constexpr int kParts = kDecodeThreads / kOct > 0 ? kDecodeThreads / kOct : 1;
-  float* part = red;  // [kParts][G * 128]
-  const int npairs = G * 64;
+  // merge the warps' partials per head: thread = (head, two columns)
 #pragma unroll 1
-  for (int e = threadIdx.x; e < kParts * kOct; e += kDecodeThreads) {
-    const int pi = e / kOct, r = e - pi * kOct;
-    const int g = r >> 4, oc = r & 15;
-    const float* w = sc + g * maxk;
-    const uint8_t* vb = kv + maxk * kRow + oc * 16;
-    const int j0 = nk * pi / kParts, j1 = nk * (pi + 1) / kParts;
-    float acc[8];
-#pragma unroll
-    for (int x = 0; x < 8; ++x) acc[x] = 0.f;
-#pragma unroll 4
-    for (int j = j0; j < j1; ++j) {
-      const uint4 u = *reinterpret_cast<const uint4*>(vb + j * kRow);
-      const float wj = w[j];
-      const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int x = 0; x < 4; ++x) {
-        const float2 f = ElemTraits<T>::unpack2(uw[x]);
-        acc[2 * x] = fmaf(wj, f.x, acc[2 * x]);
-        acc[2 * x + 1] = fmaf(wj, f.y, acc[2 * x + 1]);
-      }
-    }
-    float4* dst = reinterpret_cast<float4*>(part + pi * G * 128 + g * 128 + oc * 8);
-    dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-  }
-  __syncthreads();
-#pragma unroll 1
-  for (int r = threadIdx.x; r < npairs; r += kDecodeThreads) {
+  for (int r = threadIdx.x; r < G * 64; r += NT) {
     const int g = r >> 6, c = (r & 63) * 2;
-    float s0 = 0.f, s1 = 0.f;
+    float M = -INFINITY;
 #pragma unroll
-    for (int pi = 0; pi < kParts; ++pi) {
-      const float2 f = *reinterpret_cast<const float2*>(part + pi * G * 128 + g * 128 + c);
-      s0 += f.x;
-      s1 += f.y;
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, ml[(w * G + g) * 2]);
+    float L = 0.f, s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float mw = ml[(w * G + g) * 2];
+      const float cw = mw == -INFINITY ? 0.f : exp2f(mw - M);
+      L = fmaf(ml[(w * G + g) * 2 + 1], cw, L);
+      const float2 f = *reinterpret_cast<const float2*>(part + (w * G + g) * 128 + c);
+      s0 = fmaf(f.x, cw, s0);
+      s1 = fmaf(f.y, cw, s1);
     }
-    const float l = stat[g];
-    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const float inv = L > 0.f ? 1.f / L : 0.f;
     *reinterpret_cast<uint32_t*>(row_ptr(a.out, b, kvh * G + g, t) + c * 2) = ElemTraits<T>::pack2(s0 * inv, s1 * inv);
+    if (c == 0 && a.lse) a.lse[b * a.ls_b + (int64_t)(kvh * G + g) * a.ls_h + t] = (M + log2f(L)) * 0.6931471805599453f;
   }
 }
 
@@ -466,19 +474,14 @@ int launch_active(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4*
   }
   a.close_block = close_block;
   a.close_slot = close_slot;
-  const int maxk = window + kMaxSummaries;
-  const size_t smem = (size_t)2 * maxk * (256 + 16) + (size_t)a.G * 256 +
-                      sizeof(float) * ((size_t)a.G * maxk + (size_t)a.G * 132 +
-                                       (size_t)decode_red_floats(a.G) +
-                                       (size_t)a.G) +
-                      sizeof(int) * (1 + kMaxSummaries);
+  const size_t smem = decode_smem_bytes(a.G, window);
   dim3 grid((unsigned)a.Tq, (unsigned)(a.B * a.Hkv));
   if (grid.x == 0 || grid.y == 0) return BNA_OK;
   auto launch = [&](auto kern) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(kDecodeThreads);
+    cfg.blockDim = dim3(decode_threads(a.G));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute at[1];
