@@ -643,6 +643,31 @@ def run_decode(dev, seed, reps, warmup):
     return us, cache
 
 
+def launch_floor_us(dev, ctas: int, n: int = 128) -> float:
+    """Per-launch time of a graph of ``n`` empty dependent launches (programmatic dependent
+    launch, ``ctas`` CTAs each): the floor under a chain of decode steps."""
+    from butterfly_b200 import _lib
+    s = torch.cuda.Stream(device=dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            _lib.check(_lib.lib().bna_launch_probe(ctas, _lib.stream_ptr(dev)))
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
+            for _ in range(n):
+                _lib.check(_lib.lib().bna_launch_probe(ctas, _lib.stream_ptr(dev)))
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = _events(2)
+    e0.record()
+    for _ in range(10):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1000.0 / (10 * n)
+
+
 def run_batched_decode(ws, dev, hbm_peak, rank):
     us, cache = run_decode(dev, 2000 + rank, reps=10, warmup=3)
     us = _max_over_ranks(us, ws)
@@ -652,6 +677,8 @@ def run_batched_decode(ws, dev, hbm_peak, rank):
            "us_per_step": round(us, 3), "sequences_per_step": DEC_B * ws,
            "algorithmic_bytes_per_step": decode_bytes_per_step(),
            "achieved_gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm_peak, 4),
+           "launch_floor_us": round(launch_floor_us(dev, DEC_B * HKV), 3),
+           "launch_floor_note": "graph of 128 empty dependent launches of 128 CTAs (bna_launch_probe)",
            "retained_kv_bytes_per_layer": cache.nbytes,
            "dense_kv_bytes_per_layer": 2 * DEC_B * HKV * (DEC_CTX + DEC_STEPS) * DH * 2}
     del cache

@@ -36,6 +36,7 @@ int launch_active(const bna_tensor4*, const bna_tensor4*, const bna_tensor4*, co
                   const bna_tensor4*, int64_t, int64_t, cudaStream_t);
 int launch_selection_dump(const bna_route*, int, int32_t*, int32_t*, cudaStream_t);
 int take_device_error(int, int32_t*);
+int launch_probe(int, cudaStream_t);
 void set_prefill_trace(uint64_t*);
 
 // ---------------------------------------------------------------- validation helpers
@@ -356,3 +357,7 @@ int bna_decode_step(const bna_tensor4* q, const bna_tensor4* k_new, const bna_te
 }
 
 }  // extern "C"
+
+extern "C" BNA_API int bna_launch_probe(int32_t ctas, void* stream) {
+  return bna::launch_probe(ctas, static_cast<cudaStream_t>(stream));
+}

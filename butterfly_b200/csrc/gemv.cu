@@ -174,29 +174,27 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs a)
   for (int r = 0; r < R; ++r)
 #pragma unroll
     for (int m = 0; m < kMaxM; ++m) acc[r][m] = 0.f;
-  auto fma_chunk = [&](const uint4 (&wv)[R], int c) {
-    float wf[R][8];
-#pragma unroll
-    for (int r = 0; r < R; ++r) unpack8f(wv[r], wf[r], bf);
-#pragma unroll
-    for (int m = 0; m < kMaxM; ++m) {
-      if (m < a.M) {
-        float xf[8];
-        unpack8f(*reinterpret_cast<const uint4*>(smem + 2 * ((int64_t)m * a.K + (c * 32 + lane) * 8)), xf, bf);
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[r][m] = fmaf(wf[r][e], xf[e], acc[r][m]);
-      }
-    }
-  };
+  // acc[r][m] += W[row r, chunk c] . x_in[m, chunk c]
+#define BNA_GEMV_CHUNK(WV, C)                                                                              \
+  {                                                                                                        \
+    float wf_[R][8];                                                                                       \
+    _Pragma("unroll") for (int r = 0; r < R; ++r) unpack8f(WV[r], wf_[r], bf);                             \
+    _Pragma("unroll") for (int m = 0; m < kMaxM; ++m) {                                                    \
+      if (m < a.M) {                                                                                       \
+        float xf_[8];                                                                                      \
+        unpack8f(*reinterpret_cast<const uint4*>(smem + 2 * ((int64_t)m * a.K + ((C) * 32 + lane) * 8)), xf_, bf); \
+        _Pragma("unroll") for (int r = 0; r < R; ++r)                                                      \
+        _Pragma("unroll") for (int e = 0; e < 8; ++e) acc[r][m] = fmaf(wf_[r][e], xf_[e], acc[r][m]);      \
+      }                                                                                                    \
+    }                                                                                                      \
+  }
 #pragma unroll
   for (int c = 0; c < NPRE; ++c) {
     if (c < nch) {
       uint4 wv[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) wv[r] = wpre[r][c];
-      fma_chunk(wv, c);
+      BNA_GEMV_CHUNK(wv, c)
     }
   }
   for (int c0 = NPRE; c0 < nch; c0 += NPRE) {
@@ -212,10 +210,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs a)
         uint4 wv[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) wv[r] = wb[r][c];
-        fma_chunk(wv, c0 + c);
+        BNA_GEMV_CHUNK(wv, c0 + c)
       }
     }
   }
+#undef BNA_GEMV_CHUNK
 #pragma unroll
   for (int r = 0; r < R; ++r)
 #pragma unroll

@@ -386,6 +386,27 @@ __global__ void __launch_bounds__(decode_threads(G)) decode_kernel(const ActiveA
   }
 }
 
+// ------------------------------------------------------------------------------ launch probe
+// An empty grid launched like the decode step (programmatic dependent launch): a chain of
+// these measures the per-launch floor that a chain of decode steps cannot go below.
+__global__ void launch_probe_kernel() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+int launch_probe(int ctas, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(ctas > 0 ? ctas : 1));
+  cfg.blockDim = dim3(32);
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, launch_probe_kernel), "launch probe");
+}
+
 // ------------------------------------------------------------------------------ selection dump
 __global__ void prefill_selection_kernel(const bna_route r, int window, int32_t* idx, int32_t* cnt) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;

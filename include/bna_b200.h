@@ -92,6 +92,11 @@ BNA_API int bna_take_device_error(int device, int32_t* code_out);
  * number of SMs).  Pass NULL to stop.  Used by the profiling tools only. */
 BNA_API int bna_set_prefill_trace(void* device_buffer);
 
+/* Profiling aid: launches an empty grid of `ctas` CTAs the way the decode step is launched
+ * (programmatic dependent launch).  A graph of these gives the per-launch floor of a chain
+ * of dependent decode steps. */
+BNA_API int bna_launch_probe(int32_t ctas, void* stream);
+
 /* ---- topology / selection (host) -------------------------------------------------- */
 
 /* Fill `route` (everything but `neighbors`) for a layer; replaces
