@@ -11,13 +11,13 @@
 //
 // Each prologue/epilogue does the eager ops' arithmetic, rounding to the storage type where
 // the eager layer rounds.  The projection is HBM-bound (every weight byte is read once per
-// call): each warp owns one output row (the gate/up pair for SWIGLU) and streams it with
-// 128-bit loads, lane l taking
-// columns [8(32c + l), +8) of chunk c.  All of a warp's weight loads are issued before
-// griddepcontrol.wait, so under programmatic dependent launch the weight stream of a
-// projection overlaps the tail of the kernel that produces its input; x_in is then built
-// in shared memory by every CTA (it is a few KB) and the dot products are reduced across
-// the warp with shuffles.
+// call).  A warp owns one output (the gate/up row pair for SWIGLU) over one K segment of
+// up to 1024 columns, lane l taking columns [8(32c + l), +8) of chunk c; it issues all its
+// 128-bit weight loads before griddepcontrol.wait, so under programmatic dependent launch
+// the weight stream of a projection overlaps the tail of the kernel that produces its
+// input.  x_in is then built in shared memory by every CTA (it is a few KB), the dot
+// products are reduced across the warp with shuffles and the K segments through shared
+// memory.
 #include <cuda_runtime.h>
 
 #include <string>
@@ -137,143 +137,136 @@ __device__ __forceinline__ void build_input(const GemvArgs& a, uint8_t* xs, floa
   __syncthreads();
 }
 
-// R rows per warp (the two rows of a SWIGLU pair when EPI == SWIGLU), NPRE chunks of 256
-// columns preloaded per row before the dependency wait; further chunks are streamed.
-template <typename T, int PRO, int EPI, int R, int NPRE>
+// Warp task = (output, K segment of up to 4 chunks of 256 columns): S segments per output,
+// 8 / S outputs per CTA.  A warp preloads its (at most 4 x R) 128-bit weight loads before the
+// dependency wait, so the code each warp runs is one short straight stretch (long unrolled
+// code executed once per warp is bound by instruction fetch), and every projection
+// spreads over hundreds of CTAs.  The S segment partials of an output meet in shared memory.
+template <typename T, int PRO, int EPI, int MT, int S>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs a) {
   constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
+  constexpr int R = EPI == EPI_SWIGLU ? 2 : 1;
+  constexpr int OPC = kGemvWarps / S;  // outputs per CTA
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ float red[kGemvWarps];
+  __shared__ float part[kGemvWarps][R][MT];
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rows_per_warp = EPI == EPI_SWIGLU ? 1 : R;
-  const int o0 = (blockIdx.x * kGemvWarps + warp) * rows_per_warp;  // first output of this warp
-  const bool active = o0 < a.n_out;
+  const int ol = warp / S, seg = warp - ol * S;
+  const int o = blockIdx.x * OPC + ol;
+  const bool active = o < a.n_out;
   const int nch = (int)(a.K >> 8);
-  int64_t row[R];
+  const int c0 = seg * 4;
+  const int oc = active ? o : a.n_out - 1;  // clamp: loads stay in bounds, results dropped
+  const uint8_t* wrow[R];
+  wrow[0] = a.w + 2 * ((int64_t)oc * a.K);
+  if (R == 2) wrow[R - 1] = a.w + 2 * (((int64_t)oc + a.up_off) * a.K);
+  uint4 wv[R][4];
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    int o = EPI == EPI_SWIGLU ? o0 : o0 + r;
-    if (o >= a.n_out) o = a.n_out - 1;  // clamp: loads stay in bounds, results dropped
-    row[r] = EPI == EPI_SWIGLU ? (int64_t)o + (r ? a.up_off : 0) : (int64_t)o;
-  }
-  uint4 wpre[R][NPRE];
-  if (active) {
+  for (int c = 0; c < 4; ++c)
 #pragma unroll
-    for (int c = 0; c < NPRE; ++c)
-#pragma unroll
-      for (int r = 0; r < R; ++r)
-        if (c < nch) wpre[r][c] = ld_nc_128(a.w + 2 * (row[r] * a.K + (int64_t)(c * 32 + lane) * 8));
-  }
+    for (int r = 0; r < R; ++r)
+      if (c0 + c < nch) wv[r][c] = ld_nc_128(wrow[r] + 16 * ((c0 + c) * 32 + lane));
   // the input is produced by the previous kernel of the stream
   asm volatile("griddepcontrol.wait;" ::: "memory");
   build_input<T, PRO>(a, smem, red);
-  if (!active) return;
-  float acc[R][kMaxM];
+  float acc[R][MT];
 #pragma unroll
   for (int r = 0; r < R; ++r)
 #pragma unroll
-    for (int m = 0; m < kMaxM; ++m) acc[r][m] = 0.f;
-  // acc[r][m] += W[row r, chunk c] . x_in[m, chunk c]
-#define BNA_GEMV_CHUNK(WV, C)                                                                              \
-  {                                                                                                        \
-    float wf_[R][8];                                                                                       \
-    _Pragma("unroll") for (int r = 0; r < R; ++r) unpack8f(WV[r], wf_[r], bf);                             \
-    _Pragma("unroll") for (int m = 0; m < kMaxM; ++m) {                                                    \
-      if (m < a.M) {                                                                                       \
-        float xf_[8];                                                                                      \
-        unpack8f(*reinterpret_cast<const uint4*>(smem + 2 * ((int64_t)m * a.K + ((C) * 32 + lane) * 8)), xf_, bf); \
-        _Pragma("unroll") for (int r = 0; r < R; ++r)                                                      \
-        _Pragma("unroll") for (int e = 0; e < 8; ++e) acc[r][m] = fmaf(wf_[r][e], xf_[e], acc[r][m]);      \
-      }                                                                                                    \
-    }                                                                                                      \
-  }
+    for (int m = 0; m < MT; ++m) acc[r][m] = 0.f;
 #pragma unroll
-  for (int c = 0; c < NPRE; ++c) {
-    if (c < nch) {
-      uint4 wv[R];
+  for (int c = 0; c < 4; ++c) {
+    if (c0 + c < nch) {
+      float wf[R][8];
 #pragma unroll
-      for (int r = 0; r < R; ++r) wv[r] = wpre[r][c];
-      BNA_GEMV_CHUNK(wv, c)
-    }
-  }
-  for (int c0 = NPRE; c0 < nch; c0 += NPRE) {
-    uint4 wb[R][NPRE];
+      for (int r = 0; r < R; ++r) unpack8f(wv[r][c], wf[r], bf);
 #pragma unroll
-    for (int c = 0; c < NPRE; ++c)
+      for (int m = 0; m < MT; ++m) {
+        float xf[8];
+        unpack8f(*reinterpret_cast<const uint4*>(smem + 2 * ((int64_t)m * a.K + ((c0 + c) * 32 + lane) * 8)), xf, bf);
 #pragma unroll
-      for (int r = 0; r < R; ++r)
-        if (c0 + c < nch) wb[r][c] = ld_nc_128(a.w + 2 * (row[r] * a.K + (int64_t)((c0 + c) * 32 + lane) * 8));
+        for (int r = 0; r < R; ++r)
 #pragma unroll
-    for (int c = 0; c < NPRE; ++c) {
-      if (c0 + c < nch) {
-        uint4 wv[R];
-#pragma unroll
-        for (int r = 0; r < R; ++r) wv[r] = wb[r][c];
-        BNA_GEMV_CHUNK(wv, c0 + c)
+          for (int e = 0; e < 8; ++e) acc[r][m] = fmaf(wf[r][e], xf[e], acc[r][m]);
       }
     }
   }
-#undef BNA_GEMV_CHUNK
 #pragma unroll
   for (int r = 0; r < R; ++r)
 #pragma unroll
-    for (int m = 0; m < kMaxM; ++m)
-      if (m < a.M) {
+    for (int m = 0; m < MT; ++m) {
+      float v = acc[r][m];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc[r][m] += __shfl_xor_sync(0xffffffffu, acc[r][m], o);
-      }
-  if (lane != 0) return;
-  for (int m = 0; m < a.M; ++m) {
-    if (EPI == EPI_SWIGLU) {
-      const float g = rnd<T>(acc[0][m]), u = rnd<T>(acc[R - 1][m]);
-      const float y = rnd<T>(g / (1.f + __expf(-g))) * u;
-      *reinterpret_cast<uint16_t*>(a.out + 2 * ((int64_t)m * a.out_stride + o0)) =
-          (uint16_t)(ElemTraits<T>::pack2(y, 0.f) & 0xFFFFu);
-    } else {
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (lane == 0) part[warp][r][m] = v;
+    }
+  __syncthreads();
+  // epilogue: thread = (output of this CTA, token)
+  const int tid = threadIdx.x;
+  if (tid >= OPC * MT) return;
+  const int ole = tid / MT, m = tid - ole * MT;
+  const int oe = blockIdx.x * OPC + ole;
+  if (oe >= a.n_out || m >= a.M) return;
+  float y[R];
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int o = o0 + r;
-        if (o >= a.n_out) break;
-        float y = rnd<T>(acc[r][m]);
-        if (EPI == EPI_RESID) {
-          const uint16_t rb = *reinterpret_cast<const uint16_t*>(a.res2 + 2 * ((int64_t)m * a.res2_stride + o));
-          y = y + ElemTraits<T>::unpack2((uint32_t)rb).x;
-        }
-        *reinterpret_cast<uint16_t*>(a.out + 2 * ((int64_t)m * a.out_stride + o)) =
-            (uint16_t)(ElemTraits<T>::pack2(y, 0.f) & 0xFFFFu);
-      }
+  for (int r = 0; r < R; ++r) {
+    float t = 0.f;
+#pragma unroll
+    for (int sg = 0; sg < S; ++sg) t += part[ole * S + sg][r][m];
+    y[r] = t;
+  }
+  float out;
+  if (EPI == EPI_SWIGLU) {
+    const float g = rnd<T>(y[0]), u = rnd<T>(y[R - 1]);
+    out = rnd<T>(g / (1.f + __expf(-g))) * u;
+  } else {
+    out = rnd<T>(y[0]);
+    if (EPI == EPI_RESID) {
+      const uint16_t rb = *reinterpret_cast<const uint16_t*>(a.res2 + 2 * ((int64_t)m * a.res2_stride + oe));
+      out = out + ElemTraits<T>::unpack2((uint32_t)rb).x;
     }
   }
+  *reinterpret_cast<uint16_t*>(a.out + 2 * ((int64_t)m * a.out_stride + oe)) =
+      (uint16_t)(ElemTraits<T>::pack2(out, 0.f) & 0xFFFFu);
 }
 
-// One output row per warp (the gate/up row pair for SWIGLU), so even the 1024-row
-// projections spread over 128 CTAs; all of a row's chunks are preloaded when they fit.
-template <typename T, int PRO, int EPI>
-int launch_gemv(const GemvArgs& a, cudaStream_t s) {
-  constexpr int R = EPI == EPI_SWIGLU ? 2 : 1;
-  const int per_cta = kGemvWarps * (EPI == EPI_SWIGLU ? 1 : R);
+template <typename T, int PRO, int EPI, int MT, int S>
+int launch_gemv_ms(const GemvArgs& a, cudaStream_t s) {
+  constexpr int OPC = kGemvWarps / S;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((a.n_out + per_cta - 1) / per_cta));
+  cfg.gridDim = dim3((unsigned)((a.n_out + OPC - 1) / OPC));
   cfg.blockDim = dim3(kGemvWarps * 32);
-  cfg.dynamicSmemBytes = (size_t)a.M * a.K * 2;
+  cfg.dynamicSmemBytes = (size_t)MT * a.K * 2;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const int nch = (int)(a.K >> 8);
-  cudaError_t e;
-  constexpr int kBig = R == 1 ? 16 : 8;
-  auto kern = nch <= 4 ? gemv_kernel<T, PRO, EPI, R, 4>
-                       : (nch <= 8 ? gemv_kernel<T, PRO, EPI, R, 8> : gemv_kernel<T, PRO, EPI, R, kBig>);
+  auto kern = gemv_kernel<T, PRO, EPI, MT, S>;
   if (cfg.dynamicSmemBytes > 48 * 1024) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
     if (e != cudaSuccess) return check_cuda(e, "gemv smem attribute");
   }
-  e = cudaLaunchKernelEx(&cfg, kern, a);
-  return check_cuda(e, "gemv launch");
+  return check_cuda(cudaLaunchKernelEx(&cfg, kern, a), "gemv launch");
+}
+
+template <typename T, int PRO, int EPI, int MT>
+int launch_gemv_m(const GemvArgs& a, cudaStream_t s) {
+  const int nch = (int)(a.K >> 8);
+  if (nch <= 4) return launch_gemv_ms<T, PRO, EPI, MT, 1>(a, s);
+  if (nch <= 8) return launch_gemv_ms<T, PRO, EPI, MT, 2>(a, s);
+  if (nch <= 16) return launch_gemv_ms<T, PRO, EPI, MT, 4>(a, s);
+  return launch_gemv_ms<T, PRO, EPI, MT, 8>(a, s);
+}
+
+template <typename T, int PRO, int EPI>
+int launch_gemv(const GemvArgs& a, cudaStream_t s) {
+  if (a.M <= 1) return launch_gemv_m<T, PRO, EPI, 1>(a, s);
+  if (a.M <= 2) return launch_gemv_m<T, PRO, EPI, 2>(a, s);
+  if (a.M <= 4) return launch_gemv_m<T, PRO, EPI, 4>(a, s);
+  return launch_gemv_m<T, PRO, EPI, 8>(a, s);
 }
 
 template <int PRO, int EPI>
@@ -287,7 +280,7 @@ bool a16(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p)
 
 int check_common(const GemvArgs& a) {
   if (a.M < 1 || a.M > kMaxM) return fail(BNA_UNSUPPORTED, "gemv: 1 <= tokens <= 8");
-  if (a.K <= 0 || a.K % 256) return fail(BNA_UNSUPPORTED, "gemv: in_features must be a multiple of 256");
+  if (a.K <= 0 || a.K % 256 || a.K > 8192) return fail(BNA_UNSUPPORTED, "gemv: in_features must be a multiple of 256, <= 8192");
   if ((int64_t)a.M * a.K * 2 > 160 * 1024) return fail(BNA_UNSUPPORTED, "gemv: tokens * in_features too large");
   if (a.n_out <= 0) return fail(BNA_BAD_SHAPE, "gemv: out_features must be positive");
   if (!a.x || !a.w || !a.out) return fail(BNA_BAD_SHAPE, "gemv: null pointer");
