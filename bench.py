@@ -997,6 +997,11 @@ def profile_case(kind: str):
         for _ in range(3):
             prefill_attention_into(q, k, v, ks, vs, out, None, r, W, 1 / math.sqrt(DH))
         torch.cuda.synchronize()
+    elif kind == "prefill-128k":
+        # the model workload's attention shape (T=131072, Hq8/Hkv2): warm-up, then one launch
+        att = attention_kernel_at(dev, MODEL_T, MODEL["heads"], MODEL["kv_heads"], layer=MODEL["layers"] - 1, reps=1,
+                                  hbm_peak=_peaks()[0])
+        print(att)
     elif kind == "model-decode":
         # greedy decode tokens of the fused model after a 128k prefill, inside an NVTX range
         # named "decode" (ncu --nvtx --nvtx-include decode/)
@@ -1040,7 +1045,7 @@ def main():
     ap.add_argument("--no-layer", action="store_true", help="skip the 32k attention-layer leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the batched-decode leg")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--profile-case", choices=["prefill", "decode", "prefill-trace", "model-prefill", "model-decode"], default=None,
+    ap.add_argument("--profile-case", choices=["prefill", "decode", "prefill-trace", "model-prefill", "model-decode", "prefill-128k"], default=None,
                     help="small case for ncu: warm-up, then the launches to capture")
     args = ap.parse_args()
     if args.profile_case:
