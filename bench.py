@@ -405,6 +405,82 @@ def attention_kernel_at(dev, seq_len, hq, hkv, layer, reps, hbm_peak):
             "compressor_gbs": round(cb / (cms / 1000) / 1e9, 1), "l2": "flushed (2x L2 write) before each launch"}
 
 
+# ----------------------------------------------------------------------------- sequence shard (262k)
+SHARD_MODEL = dict(hidden=2560, layers=32, heads=16, kv_heads=4, head_dim=128, inter=9728, vocab=151936)
+SHARD_T = 262144
+
+
+def retained_kv_bytes(total: int, spec, chunk: int = MODEL_CHUNK, decode_tokens: int = 0) -> int:
+    """Bytes a two-pool cache keeps for a ``total``-token prompt handed over in ``chunk``
+    chunks, then ``decode_tokens`` one-token steps (tail rows + closed block means, K and V,
+    bf16, every layer): the same counter arithmetic the cache runs."""
+    from butterfly_b200.cache import CompressedKVCache
+    c = CompressedKVCache(block_size=BS, local_window_tokens=W, max_kv_size=total + 64, max_chunk_size=chunk)
+    c.tail_capacity = W + 2 * chunk + 2 * BS
+    c.summary_capacity = (total + 64) // BS + 4
+    c._advance_counters_chunked(total, chunk)
+    for _ in range(decode_tokens):
+        c._advance_counters_chunked(1, 1)
+    return 2 * spec["kv_heads"] * spec["head_dim"] * 2 * (c.tail_size + c.summary_count) * spec["layers"]
+
+
+def run_seq_shard(args, ws, rank, dev, peaks):
+    """The 4B-class model's 262144-token prefill, sequence-sharded over the ranks (strong
+    scaling: one sequence, T / n_gpus tokens per GPU; NCCL all-gathers of block means and
+    the W-1-token halo in every layer)."""
+    from butterfly_b200.integrations import qwen_torch as qt
+    from butterfly_b200.integrations.qwen_fused import fuse_qwen_decoder_layers
+    tc_sus = peaks[2]
+    if SHARD_T % (ws * BS):
+        return {"error": f"T={SHARD_T} does not split into whole blocks over {ws} ranks"}
+    model = build_model(dev, seed=2, spec=SHARD_MODEL)
+    fuse_qwen_decoder_layers(model)
+    Tl = SHARD_T // ws
+    g = torch.Generator().manual_seed(2000)
+    ids = torch.randint(0, SHARD_MODEL["vocab"], (1, SHARD_T), generator=g)[:, rank * Tl:(rank + 1) * Tl].to(dev)
+    pos = torch.arange(rank * Tl, (rank + 1) * Tl, device=dev).view(1, -1)
+
+    @torch.no_grad()
+    def step():
+        with qt.sequence_sharded(model, SHARD_T):
+            return model(input_ids=ids, position_ids=pos, use_cache=False, logits_to_keep=1).logits
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    n = max(1, min(3, args.steps))
+    _barrier(ws)
+    e0, e1 = _events(2)
+    e0.record()
+    for _ in range(n):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(e0.elapsed_time(e1) / n, ws)
+    flops = model_linear_flops_per_token(SHARD_MODEL) * SHARD_T + sum(
+        4 * SHARD_MODEL["head_dim"] * SHARD_MODEL["heads"] * attention_valid_keys(SHARD_T, l)
+        for l in range(SHARD_MODEL["layers"])) + 2 * SHARD_MODEL["hidden"] * SHARD_MODEL["vocab"]
+    tflops = flops / (ms / 1000.0) / 1e12
+    per_layer_exchange = 2 * SHARD_MODEL["kv_heads"] * (SHARD_T // BS) * SHARD_MODEL["head_dim"] * 2
+    out = {"workload": f"4B-class Qwen3.5 decoder (seed 2): 32 layers, hidden 2560, Hq16/Hkv4, dh128, SwiGLU 9728, "
+                       f"vocab 151936, compressed Butterfly BS128 W64 + fused glue; one {SHARD_T}-token prefill "
+                       f"sequence-sharded over {ws} GPU(s) ({Tl} tokens each), use_cache=False, logits_to_keep=1",
+           "scaling": "strong", "prefill_tok_per_s": round(SHARD_T / (ms / 1000.0), 1), "ms_per_step": round(ms, 2),
+           "steps": n, "tensor_roofline": {"achieved": round(tflops, 1), "peak": round(tc_sus * ws, 1),
+                                           "frac": round(tflops / (tc_sus * ws), 4), "unit": "TFLOP/s",
+                                           "note": "whole-job FLOPs over the measured sustained bf16 peak x n_gpus"},
+           "all_gather_bytes_per_layer": per_layer_exchange + ws * 2 * (W - 1) * SHARD_MODEL["kv_heads"] * 128 * 2,
+           "retained_kv_bytes_after_prefill": retained_kv_bytes(SHARD_T, SHARD_MODEL),
+           "retained_kv_bytes_after_one_decode_token": retained_kv_bytes(SHARD_T, SHARD_MODEL, decode_tokens=1),
+           "retained_kv_note": "two-pool cache counters for the prompt handed over in 4096-token chunks "
+                               "(kv_step of the reference harness); the tail trims to the window at the first "
+                               "decode token",
+           "dense_kv_bytes": 2 * SHARD_MODEL["kv_heads"] * SHARD_MODEL["head_dim"] * 2 * SHARD_T * SHARD_MODEL["layers"]}
+    del model
+    torch.cuda.empty_cache()
+    return out
+
+
 # ----------------------------------------------------------------------------- layer (32k)
 def _layouts(seq_len):
     import butterfly_b200 as bb
@@ -1045,6 +1121,7 @@ def main():
     ap.add_argument("--no-layer", action="store_true", help="skip the 32k attention-layer leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the batched-decode leg")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-shard", action="store_true", help="skip the sequence-sharded 262k leg")
     ap.add_argument("--profile-case", choices=["prefill", "decode", "prefill-trace", "model-prefill", "model-decode", "prefill-128k"], default=None,
                     help="small case for ncu: warm-up, then the launches to capture")
     args = ap.parse_args()
@@ -1062,6 +1139,7 @@ def main():
     hbm_peak = peaks[0]
 
     m = run_model(args, ws, rank, local, dev, peaks)
+    shard = None if args.no_shard else run_seq_shard(args, ws, rank, dev, peaks)
     layer = None if args.no_layer else run_layer(args, ws, dev, hbm_peak, rank)
     bdec = None if args.no_decode else run_batched_decode(ws, dev, hbm_peak, rank)
     cpu = None
@@ -1091,6 +1169,7 @@ def main():
         "clocks": m["clocks"],
         "decode": m["decode"],
         "prefill_unfused_glue": m["unfused"],
+        "seq_shard": shard,
         "layer": layer,
         "decode_batched": bdec,
     }

@@ -74,8 +74,8 @@ def lib() -> ctypes.CDLL:
             "bna_cache_append": (i32, [T4, T4, T4, T4, i32, i64, i64, vp]),
             "bna_prefill_attention_static_scratch": (i32, [T4, T4, T4, T4, vp, i64, i64, i32, R, i32, f32, vp]),
             "bna_rmsnorm": (i32, [vp, i64, vp, i64, vp, vp, i64, vp, i64, i64, i32, f32, i32, vp]),
-            "bna_qk_norm_rope": (i32, [vp, i64, i64, vp, i64, i64, vp, vp, vp, vp, i64, i32, vp, vp, i64, i32, i32, i32,
-                                       f32, i32, vp]),
+            "bna_qk_norm_rope": (i32, [vp, i64, i64, vp, i64, i64, vp, vp, vp, vp, i64, i32, vp, vp, vp, i64, i64, vp,
+                                       i64, i32, i32, i32, f32, i32, vp]),
             "bna_gate_sigmoid_mul": (i32, [vp, vp, i64, i64, vp, i64, i32, i32, i32, vp]),
             "bna_swiglu": (i32, [vp, i64, i64, vp, i64, i32, i32, vp]),
             "bna_gemv_rmsnorm": (i32, [vp, i64, vp, i64, vp, f32, vp, i64, vp, i64, i64, i32, vp, i64, i32, i32, vp]),

@@ -118,6 +118,9 @@ struct QKArgs {
   int rot;
   uint8_t* q_out;
   uint8_t* k_out;
+  const uint8_t* v;   // optional pass-through of V rows into v_out (same layout as k_out)
+  int64_t v_tok, v_head;
+  uint8_t* v_out;
   int64_t tokens;
   int Hq, Hkv;
   float eps;
@@ -184,6 +187,12 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_kernel(const QKArgs 
     *reinterpret_cast<uint2*>(dst + 8 * lane) = make_uint2(ElemTraits<T>::pack2(x[0], x[1]),
                                                            ElemTraits<T>::pack2(x[2], x[3]));
   }
+  if (a.v_out) {
+#pragma unroll
+    for (int h = 0; h < HKV; ++h)
+      *reinterpret_cast<uint2*>(a.v_out + 2 * ((t * HKV + h) * 128) + 8 * lane) =
+          *reinterpret_cast<const uint2*>(a.v + 2 * (t * a.v_tok + (int64_t)h * a.v_head) + 8 * lane);
+  }
 }
 
 // Few tokens (decode): one warp per (token, head) row instead, so the rows of one token are
@@ -193,8 +202,15 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_row_kernel(const QKA
   constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
   const int lane = threadIdx.x & 31;
   const int item = blockIdx.x * kWarps + (threadIdx.x >> 5);
-  if (item >= (int)a.tokens * (HQ + HKV)) return;
-  const int t = item / (HQ + HKV), h = item - t * (HQ + HKV);
+  const int NH = HQ + HKV + (a.v_out ? HKV : 0);
+  if (item >= (int)a.tokens * NH) return;
+  const int t = item / NH, h = item - t * NH;
+  if (h >= HQ + HKV) {  // V pass-through row
+    const int hv = h - HQ - HKV;
+    *reinterpret_cast<uint2*>(a.v_out + 2 * (((int64_t)t * HKV + hv) * 128) + 8 * lane) =
+        *reinterpret_cast<const uint2*>(a.v + 2 * ((int64_t)t * a.v_tok + (int64_t)hv * a.v_head) + 8 * lane);
+    return;
+  }
   const bool isq = h < HQ;
   const uint8_t* src = isq ? a.q + 2 * ((int64_t)t * a.q_tok + (int64_t)h * a.q_head)
                            : a.k + 2 * ((int64_t)t * a.k_tok + (int64_t)(h - HQ) * a.k_head);
@@ -320,8 +336,13 @@ extern "C" BNA_API int bna_qk_norm_rope(const void* q, int64_t q_tok_stride, int
                                         int64_t k_tok_stride, int64_t k_head_stride, const void* q_weight,
                                         const void* k_weight, const void* cos, const void* sin,
                                         int64_t cs_tok_stride, int32_t rot, void* q_out, void* k_out,
+                                        const void* v, int64_t v_tok_stride, int64_t v_head_stride, void* v_out,
                                         int64_t tokens, int32_t hq, int32_t hkv, int32_t head_dim, float eps,
                                         int32_t dtype, void* stream) {
+  if ((v == nullptr) != (v_out == nullptr)) return fail(BNA_BAD_SHAPE, "qk_norm_rope: v and v_out go together");
+  if (v && (v_tok_stride % 4 || v_head_stride % 4 || (reinterpret_cast<uintptr_t>(v) & 7) ||
+            (reinterpret_cast<uintptr_t>(v_out) & 7)))
+    return fail(BNA_BAD_STRIDE, "qk_norm_rope: v strides must be multiples of 4 elements, pointers 8-byte aligned");
   if (tokens < 0 || hq <= 0 || hkv < 0) return fail(BNA_BAD_SHAPE, "qk_norm_rope: bad sizes");
   if (tokens == 0) return BNA_OK;
   if (head_dim != 128) return fail(BNA_UNSUPPORTED, "qk_norm_rope: head_dim must be 128");
@@ -335,13 +356,14 @@ extern "C" BNA_API int bna_qk_norm_rope(const void* q, int64_t q_tok_stride, int
   QKArgs a{static_cast<const uint8_t*>(q), q_tok_stride, q_head_stride, static_cast<const uint8_t*>(k), k_tok_stride,
            k_head_stride, static_cast<const uint8_t*>(q_weight), static_cast<const uint8_t*>(k_weight),
            static_cast<const uint8_t*>(cos), static_cast<const uint8_t*>(sin), cs_tok_stride, rot,
-           static_cast<uint8_t*>(q_out), static_cast<uint8_t*>(k_out), tokens, hq, hkv, eps};
+           static_cast<uint8_t*>(q_out), static_cast<uint8_t*>(k_out), static_cast<const uint8_t*>(v), v_tok_stride,
+           v_head_stride, static_cast<uint8_t*>(v_out), tokens, hq, hkv, eps};
   const dim3 grid((unsigned)((tokens + kWarps - 1) / kWarps)), block(kWarps * 32);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype != BNA_BF16 && dtype != BNA_F16) return fail(BNA_BAD_DTYPE, "qk_norm_rope: bfloat16 or float16 only");
   const bool bf = dtype == BNA_BF16;
   const bool per_row = tokens <= 64;
-  const dim3 grid_rows((unsigned)((tokens * (hq + hkv) + kWarps - 1) / kWarps));
+  const dim3 grid_rows((unsigned)((tokens * (hq + hkv + (v_out ? hkv : 0)) + kWarps - 1) / kWarps));
 #define BNA_QK_CASE(HQ_, HKV_)                                                                      \
   if (hq == HQ_ && hkv == HKV_) {                                                                    \
     if (per_row) {                                                                                   \

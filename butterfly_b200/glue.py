@@ -80,10 +80,15 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: Optiona
 
 
 def qk_norm_rope(q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor,
-                 cos: torch.Tensor, sin: torch.Tensor, eps: float):
+                 cos: torch.Tensor, sin: torch.Tensor, eps: float, *, k_out: Optional[torch.Tensor] = None,
+                 v: Optional[torch.Tensor] = None, v_out: Optional[torch.Tensor] = None):
     """q [B,T,Hq,128], k [B,T,Hkv,128] (token-major, any token/head strides, dim
     contiguous; q may be the query half of a gated q_proj output) -> normalised, rotated
-    q and k as contiguous [B,T,H,128].  cos/sin [B,T,rot] (rot = rotary dims)."""
+    q and k as contiguous [B,T,H,128].  cos/sin [B,T,rot] (rot = rotary dims).
+
+    With ``k_out`` (and ``v`` / ``v_out``) the K rows (and a copy of the V rows) are written
+    into those contiguous [B,T,Hkv,128] views instead, e.g. the local part of a pre-sized
+    buffer whose leading rows hold a sequence shard's halo (B == 1)."""
     _lib.require_cuda(q, k, q_weight, k_weight, cos, sin)
     B, T, Hq, dh = q.shape
     Hkv = int(k.shape[2])
@@ -98,11 +103,21 @@ def qk_norm_rope(q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_wei
         if w.dtype != q.dtype or w.numel() != dh or not w.is_contiguous():
             raise ValueError("norm weights must be contiguous [head_dim] tensors of q's dtype")
     qo = torch.empty((B, T, Hq, dh), device=q.device, dtype=q.dtype)
-    ko = torch.empty((B, T, Hkv, dh), device=q.device, dtype=q.dtype)
+    for o in (k_out, v_out):
+        if o is not None and (tuple(o.shape) != (B, T, Hkv, dh) or not o.is_contiguous()):
+            raise ValueError("k_out / v_out must be contiguous [B,T,Hkv,128] views")
+    if (v is None) != (v_out is None):
+        raise ValueError("v and v_out go together")
+    ko = k_out if k_out is not None else torch.empty((B, T, Hkv, dh), device=q.device, dtype=q.dtype)
+    vp, vts, vhs, vop = None, 0, 0, None
+    if v is not None:
+        if v.shape != k.shape or v.stride(-1) != 1:
+            raise ValueError("v must be shaped like k with a contiguous head_dim")
+        vp, vts, vhs, vop = v.data_ptr(), _token_stride(v), v.stride(2), v_out.data_ptr()
     _lib.check(_lib.lib().bna_qk_norm_rope(
         q.data_ptr(), qts, q.stride(2), k.data_ptr(), kts, k.stride(2), q_weight.data_ptr(),
-        k_weight.data_ptr(), cs.data_ptr(), sn.data_ptr(), rot, rot, qo.data_ptr(), ko.data_ptr(), B * T, Hq, Hkv,
-        dh, float(eps), _lib.dtype_code(q.dtype), _lib.stream_ptr(q.device)))
+        k_weight.data_ptr(), cs.data_ptr(), sn.data_ptr(), rot, rot, qo.data_ptr(), ko.data_ptr(), vp, vts, vhs, vop,
+        B * T, Hq, Hkv, dh, float(eps), _lib.dtype_code(q.dtype), _lib.stream_ptr(q.device)))
     return qo, ko
 
 

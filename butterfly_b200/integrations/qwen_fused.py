@@ -91,7 +91,7 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
     src = attn.fallback
     hq, hkv, dh = st.hq, st.hkv, st.dh
     x = hidden_states
-    decode = T == 1 and B <= 8 and H % 256 == 0 and st.inter % 256 == 0
+    decode = T == 1 and B <= 8 and H % 256 == 0 and st.inter % 256 == 0 and attn._shard is None
     if decode:  # weight-streaming projections with the norms, gate and residual adds fused in
         qkv = glue.gemv_rmsnorm(x.view(B, H), self.input_layernorm.weight, self.input_layernorm.eps,
                                 st.w_qkv).view(B, 1, -1)
@@ -103,11 +103,22 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
     k_raw = qkv[..., nq:nq + hkv * dh].view(B, T, hkv, dh)
     v = qkv[..., nq + hkv * dh:].view(B, T, hkv, dh)
     cos, sin = position_embeddings
-    q, k = glue.qk_norm_rope(qg[..., :dh], k_raw, src.q_norm.weight, src.k_norm.weight, cos, sin, src.q_norm.eps)
-    qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
-    if comp_cache is None and past_key_values is not None:
-        kt, vt = past_key_values.update(kt, vt, attn.layer_idx)
-    out, backend, hit = attn.attend(qt, kt, vt, comp_cache, cache_len, k_len_after, kwargs.get("cache_position"))
+    if attn._shard is not None:
+        # sequence shard: K and V go straight into buffers whose first W-1 rows receive the
+        # previous rank's halo
+        hl = int(attn.cfg.compressed_local_window_tokens) - 1
+        k_ext = torch.empty((B, hl + T, hkv, dh), device=x.device, dtype=x.dtype)
+        v_ext = torch.empty_like(k_ext)
+        q, _ = glue.qk_norm_rope(qg[..., :dh], k_raw, src.q_norm.weight, src.k_norm.weight, cos, sin,
+                                 src.q_norm.eps, k_out=k_ext[:, hl:], v=v, v_out=v_ext[:, hl:])
+        out, backend, hit = attn.attend_sharded(q.transpose(1, 2), k_ext.transpose(1, 2), v_ext.transpose(1, 2), hl)
+    else:
+        q, k = glue.qk_norm_rope(qg[..., :dh], k_raw, src.q_norm.weight, src.k_norm.weight, cos, sin,
+                                 src.q_norm.eps)
+        qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+        if comp_cache is None and past_key_values is not None:
+            kt, vt = past_key_values.update(kt, vt, attn.layer_idx)
+        out, backend, hit = attn.attend(qt, kt, vt, comp_cache, cache_len, k_len_after, kwargs.get("cache_position"))
     if decode:
         x2 = glue.gemv_gated(out.transpose(1, 2).reshape(B, hq, dh), qg[:, 0, :, dh:], src.o_proj.weight,
                              residual=x.view(B, H))

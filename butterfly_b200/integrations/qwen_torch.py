@@ -21,6 +21,7 @@ decode step is one fused append + block-close + attention launch.
 """
 from __future__ import annotations
 
+import contextlib
 import copy
 import importlib
 import math
@@ -368,6 +369,7 @@ class QwenCUDAButterflyAttention(nn.Module):
         self.hidden_size = fallback_attention.q_proj.in_features
         self._layouts: "OrderedDict[int, Any]" = OrderedDict()
         self.last_profile: Dict[str, Any] = {}
+        self._shard: Optional["SequenceShard"] = None
 
     # -- layouts (reference _get_or_build_cache :1039-1058, keyed by sequence length) --
     def _layout(self, seq_len: int):
@@ -406,6 +408,12 @@ class QwenCUDAButterflyAttention(nn.Module):
     def plan(self, q_len: int, attention_mask, past_key_values, output_attentions: bool = False):
         """(fallback reason or None, this layer's two-pool cache or None, cached length,
         key length after this call) — the routing decision of ``forward``."""
+        if self._shard is not None:
+            if _cache_seq_len(past_key_values, self.layer_idx) or isinstance(past_key_values, CompressedButterflyCache):
+                raise RuntimeError("a sequence-sharded forward is a prefill without a cache (pass use_cache=False)")
+            if self.training or (output_attentions and self.cfg.fallback_on_output_attentions):
+                raise RuntimeError("a sequence-sharded forward runs only the compressed kernels (eval, no attentions)")
+            return None, None, 0, self._shard.total_len
         comp_cache = None
         if isinstance(past_key_values, CompressedButterflyCache):
             comp_cache = past_key_values.compressed.get(int(self.layer_idx)) if self.layer_idx is not None else None
@@ -457,6 +465,22 @@ class QwenCUDAButterflyAttention(nn.Module):
             backend = "compressed_butterfly"
         return out, backend, hit
 
+    def attend_sharded(self, q, k_ext, v_ext, halo: int):
+        """Sequence-sharded prefill of this rank's queries q [B,Hq,T_local,dh]: k_ext / v_ext
+        [B,Hkv,halo+T_local,dh] hold the local keys / values at rows [halo, ...); the block
+        means and the previous rank's last ``halo`` rows are exchanged over the shard's
+        process group (NCCL all-gathers) and the kernel runs on global positions."""
+        from .. import seqshard
+        sh = self._shard
+        W = int(self.cfg.compressed_local_window_tokens)
+        Tl = int(q.shape[2])
+        lay, hit = self._layout(sh.total_len)
+        seqshard.check_shard(Tl, int(lay.block_size), W, sh.world, lay)
+        ops = seqshard.cuda_ops(lay, W, 1.0 / math.sqrt(self.head_dim))
+        ks, vs, ka, va, kv_pos0 = seqshard.shard_exchange(k_ext, v_ext, halo, int(lay.block_size), ops, sh.group)
+        out = ops.attend(q, ka, va, ks, vs, sh.rank * Tl, kv_pos0, sh.total_len)
+        return out, "compressed_sequence_shard", hit
+
     def _profile(self, q_len, k_len_after, backend, hit, t0, fused=False):
         self.last_profile = {
             "mode": "butterfly", "reason": None, "layer_idx": self.layer_idx, "seq_len": q_len,
@@ -478,16 +502,59 @@ class QwenCUDAButterflyAttention(nn.Module):
                                  attention_mask=attention_mask, past_key_values=past_key_values,
                                  cache_position=cache_position, **kwargs)
         t0 = time.perf_counter()
-        hf_cache = None if comp_cache is not None else past_key_values
+        hf_cache = None if comp_cache is not None or self._shard is not None else past_key_values
         q, k, v, gate = extract_qkv_from_qwen_attention(self.fallback, hidden_states, position_embeddings,
                                                         past_key_values=hf_cache, cache_position=cache_position)
-        out, backend, hit = self.attend(q, k, v, comp_cache, cache_len, k_len_after, cache_position)
+        if self._shard is not None:
+            h = int(self.cfg.compressed_local_window_tokens) - 1
+            B, Hkv, Tl, dh = k.shape
+            k_ext = torch.empty((B, h + Tl, Hkv, dh), device=k.device, dtype=k.dtype).transpose(1, 2)
+            v_ext = torch.empty_like(k_ext.transpose(1, 2)).transpose(1, 2)
+            k_ext[:, :, h:].copy_(k)
+            v_ext[:, :, h:].copy_(v)
+            out, backend, hit = self.attend_sharded(q, k_ext, v_ext, h)
+        else:
+            out, backend, hit = self.attend(q, k, v, comp_cache, cache_len, k_len_after, cache_position)
         input_shape = hidden_states.shape[:-1]
         attn_output = out.transpose(1, 2).reshape(*input_shape, -1)  # storage is already [B, T, Hq, dh]
         attn_output = attn_output * torch.sigmoid(gate)
         attn_output = self.fallback.o_proj(attn_output)
         self._profile(q_len, k_len_after, backend, hit, t0)
         return attn_output, None
+
+
+@dataclass
+class SequenceShard:
+    """This process's part of a sequence-sharded prefill: contiguous whole blocks of a
+    ``total_len``-token sequence, rank ``rank`` of ``world`` in process group ``group``."""
+
+    group: Any
+    rank: int
+    world: int
+    total_len: int
+
+
+@contextlib.contextmanager
+def sequence_sharded(model: nn.Module, total_len: int, group=None):
+    """Run the swapped layers' prefill sequence-sharded across the ranks of ``group``.
+
+    Inside the context every rank calls the model on its own contiguous token shard
+    ``input_ids[:, rank*T_local:(rank+1)*T_local]`` with global ``position_ids`` and
+    ``use_cache=False``; each swapped layer exchanges only its block means and a W-1-token
+    halo of K/V with the other ranks (NCCL all-gathers) and computes exactly the unsharded
+    result for its queries.  The last rank holds the next-token logits."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    sh = SequenceShard(group=group, rank=rank, world=world, total_len=int(total_len))
+    layers = list(iter_qwen_butterfly_layers(model))
+    for l in layers:
+        l._shard = sh
+    try:
+        yield sh
+    finally:
+        for l in layers:
+            l._shard = None
 
 
 # ----------------------------------------------------------------------------- swap API
@@ -547,7 +614,7 @@ swap_qwen_attention_with_wayfinder_cuda = swap_qwen_attention_with_butterfly_cud
 
 __all__ = [
     "QwenCUDAButterflyConfig", "QwenCUDAButterflyAttention", "CompressedButterflyCache", "GraphedGreedyDecode",
-    "compressed_config",
+    "SequenceShard", "compressed_config", "sequence_sharded",
     "extract_qkv_from_qwen_attention", "iter_qwen_butterfly_layers", "make_compressed_cache",
     "restore_qwen_dense_attention", "swap_qwen_attention_with_butterfly_cuda",
 ]

@@ -68,6 +68,37 @@ def _all_gather(x: torch.Tensor, world: int, group) -> torch.Tensor:
     return out.view((world,) + tuple(x.shape))
 
 
+def shard_exchange(k_ext: torch.Tensor, v_ext: torch.Tensor, halo: int, block_size: int, ops: ShardOps,
+                   group=None):
+    """The two exchanges of a sequence-sharded layer, on pre-sized K/V buffers.
+
+    ``k_ext`` / ``v_ext`` [B, Hkv, halo + T_local, dh] hold this rank's keys / values at
+    rows [halo, halo + T_local) (global positions rank * T_local onwards); their first
+    ``halo`` rows are filled here with the previous rank's last ``halo`` rows (rank 0 leaves
+    them unused).  Returns (global K summaries, global V summaries, the K/V views the
+    attention reads, their global start position)."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    h = int(halo)
+    B, Hkv, Tx, dh = k_ext.shape
+    Tl = Tx - h
+    k, v = k_ext[:, :, h:], v_ext[:, :, h:]
+    # 1. local summaries -> global summaries (rank-major blocks == global block order)
+    ks_l = ops.summaries(k, block_size)
+    vs_l = ops.summaries(v, block_size)
+    g = _all_gather(torch.stack([ks_l, vs_l]), world, group)       # [world, 2, B, Hkv, Nl, dh]
+    g = g.permute(1, 2, 3, 0, 4, 5).reshape(2, B, Hkv, world * ks_l.shape[2], dh)
+    # 2. halo: the last h rows of every rank; rank r uses rank r - 1's, written in place
+    if h > 0 and world > 1:
+        hg = _all_gather(torch.stack([k[:, :, Tl - h:], v[:, :, Tl - h:]]), world, group)
+        if rank > 0:
+            k_ext[:, :, :h].copy_(hg[rank - 1, 0])
+            v_ext[:, :, :h].copy_(hg[rank - 1, 1])
+    if rank > 0 and h > 0:
+        return g[0], g[1], k_ext, v_ext, rank * Tl - h
+    return g[0], g[1], k, v, 0
+
+
 def sequence_sharded_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layout,
                              local_window_tokens: int, ops: ShardOps, group=None) -> torch.Tensor:
     """Compressed Butterfly prefill of this rank's token shard.
@@ -75,37 +106,30 @@ def sequence_sharded_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, 
     q [B, Hq, T_local, dh], k / v [B, Hkv, T_local, dh] hold global positions
     [rank * T_local, (rank + 1) * T_local).  T_local must be a multiple of the block size and
     equal on every rank; ``layout`` describes the whole sequence (world * T_local tokens).
-    Returns this rank's [B, Hq, T_local, dh] output.
+    Returns this rank's [B, Hq, T_local, dh] output.  K and V are staged into buffers with
+    W - 1 leading halo rows (one copy of the local rows); callers that can produce K / V
+    straight into such buffers use ``shard_exchange`` directly and skip that copy.
     """
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
     B, Hq, Tl, dh = q.shape
     BS = int(layout.block_size)
     W = int(local_window_tokens)
+    check_shard(Tl, BS, W, world, layout)
+    h = W - 1
+    Hkv = int(k.shape[1])
+    k_ext = torch.empty((B, Hkv, h + Tl, dh), dtype=k.dtype, device=k.device)
+    v_ext = torch.empty_like(k_ext)
+    k_ext[:, :, h:].copy_(k)
+    v_ext[:, :, h:].copy_(v)
+    ks, vs, ka, va, kv_pos0 = shard_exchange(k_ext, v_ext, h, BS, ops, group)
+    return ops.attend(q, ka, va, ks, vs, rank * Tl, kv_pos0, world * Tl)
+
+
+def check_shard(Tl: int, BS: int, W: int, world: int, layout) -> None:
     if Tl % BS != 0:
         raise ValueError(f"each rank must own whole blocks: T_local={Tl} is not a multiple of {BS}")
-    total = world * Tl
-    if int(layout.num_blocks) != total // BS:
+    if int(layout.num_blocks) != world * Tl // BS:
         raise ValueError("layout must describe the whole sharded sequence")
     if W - 1 > Tl:
         raise ValueError("the local window must not reach past the previous rank")
-    # 1. local summaries -> global summaries (rank-major blocks == global block order)
-    ks_l = ops.summaries(k, BS)
-    vs_l = ops.summaries(v, BS)
-    kv_sum = torch.stack([ks_l, vs_l])                        # [2, B, Hkv, Nl, dh]
-    g = _all_gather(kv_sum, world, group)                     # [world, 2, B, Hkv, Nl, dh]
-    g = g.permute(1, 2, 3, 0, 4, 5).reshape(2, B, k.shape[1], world * ks_l.shape[2], dh)
-    ks, vs = g[0], g[1]
-    # 2. halo: last W - 1 keys / values of every rank; rank r uses rank r - 1's
-    h = W - 1
-    if h > 0 and world > 1:
-        halo = torch.stack([k[:, :, Tl - h:], v[:, :, Tl - h:]])   # [2, B, Hkv, h, dh]
-        hg = _all_gather(halo, world, group)
-    if rank > 0 and h > 0:
-        k_ext = torch.cat([hg[rank - 1, 0], k], dim=2)
-        v_ext = torch.cat([hg[rank - 1, 1], v], dim=2)
-        kv_pos0 = rank * Tl - h
-    else:
-        k_ext, v_ext, kv_pos0 = k, v, 0
-    # 3. local queries over the extended window and the global summaries
-    return ops.attend(q, k_ext, v_ext, ks, vs, rank * Tl, kv_pos0, total)

@@ -209,12 +209,16 @@ BNA_API int bna_rmsnorm(const void* x, int64_t x_stride, const void* res, int64_
  * rotate-half form with cos/sin [tokens, rot] (row stride cs_tok_stride), the remaining dims
  * passed through.  Source row (t, h) of q is at q + t*q_tok_stride + h*q_head_stride (so the
  * query half of a gated q_proj output is read in place); outputs are contiguous
- * [tokens, hq, head_dim] and [tokens, hkv, head_dim].  head_dim must be 128. */
+ * [tokens, hq, head_dim] and [tokens, hkv, head_dim].  With v / v_out non-NULL the V rows
+ * (strided like k) are also copied to v_out [tokens, hkv, head_dim] (so that K and V can be
+ * produced straight into pre-sized buffers, e.g. after a sequence shard's halo rows).
+ * head_dim must be 128. */
 BNA_API int bna_qk_norm_rope(const void* q, int64_t q_tok_stride, int64_t q_head_stride, const void* k,
                              int64_t k_tok_stride, int64_t k_head_stride, const void* q_weight, const void* k_weight,
                              const void* cos, const void* sin, int64_t cs_tok_stride, int32_t rot, void* q_out,
-                             void* k_out, int64_t tokens, int32_t hq, int32_t hkv, int32_t head_dim, float eps,
-                             int32_t dtype, void* stream);
+                             void* k_out, const void* v, int64_t v_tok_stride, int64_t v_head_stride, void* v_out,
+                             int64_t tokens, int32_t hq, int32_t hkv, int32_t head_dim, float eps, int32_t dtype,
+                             void* stream);
 
 /* out[t, h*head_dim + d] = o[t, h, d] * sigmoid(gate[t, h, d]); o contiguous
  * [tokens, heads, head_dim], gate strided (the gate half of a gated q_proj output). */
