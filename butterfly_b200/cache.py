@@ -215,9 +215,13 @@ class CompressedKVCache:
         return (out, lse) if return_lse else out
 
     def decode_step(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, layout, *,
-                    scale: Optional[float] = None, return_lse: bool = False):
+                    scale: Optional[float] = None, return_lse: bool = False, qk_prep=None):
         """One fused launch: append one token per sequence, close a block if one completes,
-        trim, and attend q [B,Hq,1,dh] at the new position."""
+        trim, and attend q [B,Hq,1,dh] at the new position.
+
+        With ``qk_prep = (q_norm_weight, k_norm_weight, cos, sin, eps)`` q and k_new are the
+        raw projection rows: the launch also applies the Qwen3.5 q/k RMSNorm and the rotary
+        embedding (cos / sin [B,1,rot]) before appending and attending."""
         _lib.require_cuda(q, k_new, v_new)
         B, Hq, Tq, dh = q.shape
         if Tq != 1 or k_new.shape[2] != 1:
@@ -241,10 +245,23 @@ class CompressedKVCache:
         lp, lb, lh = _lse_args(lse)
         sc = float(scale) if scale is not None else 1.0 / math.sqrt(dh)
         ts = [_lib.t4(x) for x in (q, k_new, v_new, self._tail_k, self._tail_v, self._sum_k, self._sum_v, out)]
-        _lib.check(_lib.lib().bna_decode_step(
-            *(ctypes.byref(t) for t in ts), lp, lb, lh, _lib.dtype_code(q.dtype), ctypes.byref(route),
-            self.local_window_tokens, pos, self.ring, close_block, close_slot, limit, sc,
-            _lib.stream_ptr(q.device)))
+        if qk_prep is None:
+            _lib.check(_lib.lib().bna_decode_step(
+                *(ctypes.byref(t) for t in ts), lp, lb, lh, _lib.dtype_code(q.dtype), ctypes.byref(route),
+                self.local_window_tokens, pos, self.ring, close_block, close_slot, limit, sc,
+                _lib.stream_ptr(q.device)))
+        else:
+            qw, kw, cos, sin, eps = qk_prep
+            rot = int(cos.shape[-1])
+            if cos.stride(-1) != 1 or sin.stride() != cos.stride() or int(cos.shape[0]) not in (1, B):
+                raise ValueError("cos / sin must be [B or 1, 1, rot] with contiguous rows and equal strides")
+            if qw.dtype != q.dtype or kw.dtype != q.dtype or not qw.is_contiguous() or not kw.is_contiguous():
+                raise ValueError("q / k norm weights must be contiguous and of q's dtype")
+            cs_b = int(cos.stride(0)) if int(cos.shape[0]) > 1 else 0
+            _lib.check(_lib.lib().bna_decode_step_qk(
+                *(ctypes.byref(t) for t in ts), lp, lb, lh, _lib.dtype_code(q.dtype), ctypes.byref(route),
+                self.local_window_tokens, pos, self.ring, close_block, close_slot, limit, sc, qw.data_ptr(),
+                kw.data_ptr(), cos.data_ptr(), sin.data_ptr(), cs_b, rot, float(eps), _lib.stream_ptr(q.device)))
         if closes:
             self.summary_count += 1
             self.summary_offset += self.block_size

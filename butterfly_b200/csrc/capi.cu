@@ -33,7 +33,7 @@ int launch_append(bna_tensor4*, bna_tensor4*, const bna_tensor4*, const bna_tens
 int launch_active(const bna_tensor4*, const bna_tensor4*, const bna_tensor4*, const bna_tensor4*,
                   const bna_tensor4*, bna_tensor4*, float*, int64_t, int64_t, int, const bna_route*, int,
                   const int64_t*, int64_t, int64_t, int64_t, int64_t, int, float, const bna_tensor4*,
-                  const bna_tensor4*, int64_t, int64_t, cudaStream_t);
+                  const bna_tensor4*, int64_t, int64_t, cudaStream_t, const QKPrep* = nullptr);
 int launch_selection_dump(const bna_route*, int, int32_t*, int32_t*, cudaStream_t);
 int take_device_error(int, int32_t*);
 int launch_probe(int, cudaStream_t);
@@ -328,11 +328,11 @@ int bna_cache_append(bna_tensor4* ring_k, bna_tensor4* ring_v, const bna_tensor4
   return launch_append(ring_k, ring_v, src_k, src_v, pos0, ring, (cudaStream_t)stream);
 }
 
-int bna_decode_step(const bna_tensor4* q, const bna_tensor4* k_new, const bna_tensor4* v_new, bna_tensor4* ring_k,
+static int decode_step_impl(const bna_tensor4* q, const bna_tensor4* k_new, const bna_tensor4* v_new, bna_tensor4* ring_k,
                     bna_tensor4* ring_v, bna_tensor4* sum_k, bna_tensor4* sum_v, bna_tensor4* out, float* lse,
                     int64_t lse_stride_b, int64_t lse_stride_h, int32_t dtype, const bna_route* route, int32_t window,
                     int64_t pos, int64_t ring, int64_t close_block, int64_t close_slot, int32_t num_summary_limit,
-                    float scale, void* stream) {
+                    float scale, void* stream, const QKPrep* prep) {
   if (int rc = check_active_common(q, ring_k, ring_v, sum_k, sum_v, out, dtype, route, window)) return rc;
   if (null4(k_new) || null4(v_new)) return fail(BNA_BAD_SHAPE, "null new token");
   if (int rc = check_rows(k_new, "k_new", 128)) return rc;
@@ -353,7 +353,36 @@ int bna_decode_step(const bna_tensor4* q, const bna_tensor4* k_new, const bna_te
   if (num_summary_limit > sum_k->size[2]) return fail(BNA_BAD_SHAPE, "num_summary_limit exceeds the summary pool");
   return launch_active(q, ring_k, ring_v, sum_k, sum_v, out, lse, lse_stride_b, lse_stride_h, dtype, route, window,
                        nullptr, pos, 0, ring, pos + 1, num_summary_limit, scale, k_new, v_new, close_block, close_slot,
-                       (cudaStream_t)stream);
+                       (cudaStream_t)stream, prep);
+}
+
+
+int bna_decode_step(const bna_tensor4* q, const bna_tensor4* k_new, const bna_tensor4* v_new, bna_tensor4* ring_k,
+                    bna_tensor4* ring_v, bna_tensor4* sum_k, bna_tensor4* sum_v, bna_tensor4* out, float* lse,
+                    int64_t lse_stride_b, int64_t lse_stride_h, int32_t dtype, const bna_route* route, int32_t window,
+                    int64_t pos, int64_t ring, int64_t close_block, int64_t close_slot, int32_t num_summary_limit,
+                    float scale, void* stream) {
+  return decode_step_impl(q, k_new, v_new, ring_k, ring_v, sum_k, sum_v, out, lse, lse_stride_b, lse_stride_h, dtype,
+                          route, window, pos, ring, close_block, close_slot, num_summary_limit, scale, stream, nullptr);
+}
+
+int bna_decode_step_qk(const bna_tensor4* q_raw, const bna_tensor4* k_raw, const bna_tensor4* v_new,
+                       bna_tensor4* ring_k, bna_tensor4* ring_v, bna_tensor4* sum_k, bna_tensor4* sum_v,
+                       bna_tensor4* out, float* lse, int64_t lse_stride_b, int64_t lse_stride_h, int32_t dtype,
+                       const bna_route* route, int32_t window, int64_t pos, int64_t ring, int64_t close_block,
+                       int64_t close_slot, int32_t num_summary_limit, float scale, const void* q_norm_weight,
+                       const void* k_norm_weight, const void* cos, const void* sin, int64_t cs_batch_stride,
+                       int32_t rot, float eps, void* stream) {
+  if (!q_norm_weight || !k_norm_weight) return fail(BNA_BAD_SHAPE, "decode_step_qk: null norm weight");
+  if (rot < 0 || rot > 128 || rot % 8) return fail(BNA_UNSUPPORTED, "decode_step_qk: rotary dims must be a multiple of 8 <= 128");
+  if (rot && (!cos || !sin)) return fail(BNA_BAD_SHAPE, "decode_step_qk: null cos / sin");
+  for (const void* p : {q_norm_weight, k_norm_weight, cos, sin})
+    if (p && (reinterpret_cast<uintptr_t>(p) & 7)) return fail(BNA_BAD_STRIDE, "decode_step_qk: pointers must be 8-byte aligned");
+  if (cs_batch_stride % 4) return fail(BNA_BAD_STRIDE, "decode_step_qk: cos/sin batch stride must be a multiple of 4");
+  QKPrep prep{q_norm_weight, k_norm_weight, cos, sin, cs_batch_stride, rot, eps};
+  return decode_step_impl(q_raw, k_raw, v_new, ring_k, ring_v, sum_k, sum_v, out, lse, lse_stride_b, lse_stride_h,
+                          dtype, route, window, pos, ring, close_block, close_slot, num_summary_limit, scale, stream,
+                          &prep);
 }
 
 }  // extern "C"

@@ -59,6 +59,47 @@ template <> struct ElemTraits<__half> {
   }
 };
 
+// Round to the 16-bit storage type and back (what a torch op on bf16/fp16 tensors does to
+// its fp32 result).
+template <typename T>
+__device__ __forceinline__ float round_to(float x) {
+  const uint32_t p = ElemTraits<T>::pack2(x, 0.f);
+  return ElemTraits<T>::unpack2(p).x;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// One 128-dim head row held by a warp (lane l: dims 4l..4l+3): Qwen3.5 RMSNorm
+// (x * rsqrt(mean(x^2) + eps) * (1 + w), fp32, rounded) followed by the rotary embedding in
+// rotate-half form on the first 8 * half_lanes * 2 dims with cos/sin c/s (each product and
+// the sum rounded to the storage type, as the eager bf16 ops).
+template <typename T>
+__device__ __forceinline__ void qk_row(float (&x)[4], const float (&w)[4], float eps, int lane, int half_lanes,
+                                       const float (&c)[4], const float (&s)[4]) {
+  const float ss = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
+  const float r = rsqrtf(ss * (1.f / 128.f) + eps);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) x[e] = round_to<T>((x[e] * r) * (1.f + w[e]));
+  // rotate-half partner of dim d (d < rot): d + rot/2 for the first half, d - rot/2 after
+  const bool in_rot = lane < 2 * half_lanes;
+  const bool first = lane < half_lanes;
+  const int src_lane = in_rot ? (first ? lane + half_lanes : lane - half_lanes) : lane;
+  float p[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) p[e] = __shfl_sync(0xffffffffu, x[e], src_lane);
+  if (in_rot) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float rh = first ? -p[e] : p[e];
+      x[e] = round_to<T>(round_to<T>(x[e] * c[e]) + round_to<T>(rh * s[e]));
+    }
+  }
+}
+
 __device__ __forceinline__ uint4 ld_nc_128(const void* p) {
   uint4 r;
   asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -82,6 +123,17 @@ __device__ __forceinline__ void st_256(void* p, const uint32_t* v) {
                "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
                : "memory");
 }
+
+// Fused q/k preparation of a decode step (see bna_decode_step_qk).
+struct QKPrep {
+  const void* q_weight;
+  const void* k_weight;
+  const void* cos;
+  const void* sin;
+  int64_t cs_b;
+  int rot;
+  float eps;
+};
 
 // Host-side error reporting (thread-local last error string).
 void set_error(const std::string& msg);

@@ -22,18 +22,6 @@ namespace {
 
 constexpr int kWarps = 8;  // warps per CTA of the row kernels
 
-template <typename T>
-__device__ __forceinline__ float round_to(float x) {
-  const uint32_t p = ElemTraits<T>::pack2(x, 0.f);
-  return ElemTraits<T>::unpack2(p).x;
-}
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-
 __device__ __forceinline__ void unpack8(const uint4& u, float* f, bool bf) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -125,29 +113,6 @@ struct QKArgs {
   int Hq, Hkv;
   float eps;
 };
-
-template <typename T>
-__device__ __forceinline__ void qk_row(float (&x)[4], const float (&w)[4], float eps, int lane, int half_lanes,
-                                       const float (&c)[4], const float (&s)[4]) {
-  const float ss = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
-  const float r = rsqrtf(ss * (1.f / 128.f) + eps);
-#pragma unroll
-  for (int e = 0; e < 4; ++e) x[e] = round_to<T>((x[e] * r) * (1.f + w[e]));
-  // rotate-half partner of dim d (d < rot): d + rot/2 for the first half, d - rot/2 after
-  const bool in_rot = lane < 2 * half_lanes;
-  const bool first = lane < half_lanes;
-  const int src_lane = in_rot ? (first ? lane + half_lanes : lane - half_lanes) : lane;
-  float p[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) p[e] = __shfl_sync(0xffffffffu, x[e], src_lane);
-  if (in_rot) {
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float rh = first ? -p[e] : p[e];
-      x[e] = round_to<T>(round_to<T>(x[e] * c[e]) + round_to<T>(rh * s[e]));
-    }
-  }
-}
 
 __device__ __forceinline__ void unpack4(const uint2& u, float (&f)[4], bool bf) {
   const float2 a = bf ? ElemTraits<__nv_bfloat16>::unpack2(u.x) : ElemTraits<__half>::unpack2(u.x);

@@ -151,6 +151,17 @@ struct ActiveArgs {
   const void* vnew;
   int64_t kn_b, kn_h, vn_b, vn_h;
   int64_t close_block, close_slot;
+  // fused q/k preparation of a decode step (qk_prep != 0): q and k_new are the raw
+  // projection rows; each gets the Qwen3.5 RMSNorm (weights qn_w / kn_w) and the rotary
+  // embedding (cos / sin of sequence b at cs + b * cs_b, rot dims) in the kernel
+  int qk_prep;
+  const void* qn_w;
+  const void* kn_w;
+  const void* cs;
+  const void* sn;
+  int64_t cs_b;
+  int rot;
+  float qk_eps;
   // routed summaries precomputed on the host (decode step: one known position); -1: on device
   int host_ns;
   int host_ids[kMaxSummaries];
@@ -300,6 +311,34 @@ __global__ void __launch_bounds__(decode_threads(G)) decode_kernel(const ActiveA
   }
   cp_async_wait_all();
   __syncthreads();
+  if (a.qk_prep) {
+    // warp r normalises and rotates query row r (r < G) or, for r == G, the new key row
+#pragma unroll 1
+    for (int r = warp; r <= G; r += NW) {
+      uint8_t* row = r < G ? qraw + r * 256 : kv + (nraw - 1) * 256;
+      const uint8_t* wp = static_cast<const uint8_t*>(r < G ? a.qn_w : a.kn_w);
+      const uint2 u = *reinterpret_cast<const uint2*>(row + 8 * lane);
+      const uint2 uw = *reinterpret_cast<const uint2*>(wp + 8 * lane);
+      float x[4], w[4], c[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+      const float2 x0 = ElemTraits<T>::unpack2(u.x), x1 = ElemTraits<T>::unpack2(u.y);
+      const float2 w0 = ElemTraits<T>::unpack2(uw.x), w1 = ElemTraits<T>::unpack2(uw.y);
+      x[0] = x0.x; x[1] = x0.y; x[2] = x1.x; x[3] = x1.y;
+      w[0] = w0.x; w[1] = w0.y; w[2] = w1.x; w[3] = w1.y;
+      const int half_lanes = a.rot >> 3;
+      if (lane < 2 * half_lanes) {
+        const uint8_t* cb = static_cast<const uint8_t*>(a.cs) + 2 * (b * a.cs_b) + 8 * lane;
+        const uint8_t* sb = static_cast<const uint8_t*>(a.sn) + 2 * (b * a.cs_b) + 8 * lane;
+        const uint2 uc = *reinterpret_cast<const uint2*>(cb), us = *reinterpret_cast<const uint2*>(sb);
+        const float2 c0 = ElemTraits<T>::unpack2(uc.x), c1 = ElemTraits<T>::unpack2(uc.y);
+        const float2 s0 = ElemTraits<T>::unpack2(us.x), s1 = ElemTraits<T>::unpack2(us.y);
+        c[0] = c0.x; c[1] = c0.y; c[2] = c1.x; c[3] = c1.y;
+        sn[0] = s0.x; sn[1] = s0.y; sn[2] = s1.x; sn[3] = s1.y;
+      }
+      qk_row<T>(x, w, a.qk_eps, lane, half_lanes, c, sn);
+      *reinterpret_cast<uint2*>(row + 8 * lane) = make_uint2(ElemTraits<T>::pack2(x[0], x[1]), ElemTraits<T>::pack2(x[2], x[3]));
+    }
+    __syncthreads();
+  }
   if (a.knew && threadIdx.x < 32) {
     // fused append: the new token (staged as the last window row) goes to ring slot
     // p % ring; any block close above has already read the ring
@@ -454,8 +493,19 @@ int launch_active(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4*
                   const bna_tensor4* vs, bna_tensor4* out, float* lse, int64_t ls_b, int64_t ls_h, int dtype,
                   const bna_route* route, int window, const int64_t* positions, int64_t pos0, int64_t kv_pos0,
                   int64_t ring, int64_t kv_len, int num_summary_limit, float scale, const bna_tensor4* knew,
-                  const bna_tensor4* vnew, int64_t close_block, int64_t close_slot, cudaStream_t stream) {
+                  const bna_tensor4* vnew, int64_t close_block, int64_t close_slot, cudaStream_t stream,
+                  const QKPrep* prep) {
   ActiveArgs a{};
+  if (prep) {
+    a.qk_prep = 1;
+    a.qn_w = prep->q_weight;
+    a.kn_w = prep->k_weight;
+    a.cs = prep->cos;
+    a.sn = prep->sin;
+    a.cs_b = prep->cs_b;
+    a.rot = prep->rot;
+    a.qk_eps = prep->eps;
+  }
   a.host_ns = -1;
   if (!positions && q->size[2] == 1 && route->neighbors == nullptr) {
     // one query at a known position: route it here (same selection code as the device)

@@ -18,9 +18,9 @@ rotary-embedding concatenations, separate sigmoid / SiLU / multiply / residual p
 
 For a decode step (one token per sequence, up to 8 sequences) the projections are instead
 weight-streaming GEMV kernels with the neighbouring steps fused in: rmsnorm+qkv,
-gate+o_proj+residual, rmsnorm+gate/up+SwiGLU, down_proj+residual (plus q/k norm+RoPE and
-the fused cache decode step): six launches per layer, each overlapping the previous one's
-tail through programmatic dependent launch.
+gate+o_proj+residual, rmsnorm+gate/up+SwiGLU, down_proj+residual, and the cache decode
+step with the q/k norm + RoPE of the new token fused in: five launches per layer, each
+overlapping the previous one's tail through programmatic dependent launch.
 
 The projection weights are moved into one buffer per layer ([Wq; Wk; Wv] and [Wg; Wu]) and
 the modules' ``weight`` parameters become views of it, so the model's parameters, its
@@ -112,6 +112,11 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
         q, _ = glue.qk_norm_rope(qg[..., :dh], k_raw, src.q_norm.weight, src.k_norm.weight, cos, sin,
                                  src.q_norm.eps, k_out=k_ext[:, hl:], v=v, v_out=v_ext[:, hl:])
         out, backend, hit = attn.attend_sharded(q.transpose(1, 2), k_ext.transpose(1, 2), v_ext.transpose(1, 2), hl)
+    elif decode and comp_cache is not None and cache_len > 0:
+        # one launch: q/k norm + RoPE of the new token, append, block close and attention
+        prep = (src.q_norm.weight, src.k_norm.weight, cos, sin, src.q_norm.eps)
+        out, backend, hit = attn.attend(qg[..., :dh].transpose(1, 2), k_raw.transpose(1, 2), v.transpose(1, 2),
+                                        comp_cache, cache_len, k_len_after, qk_prep=prep)
     else:
         q, k = glue.qk_norm_rope(qg[..., :dh], k_raw, src.q_norm.weight, src.k_norm.weight, cos, sin,
                                  src.q_norm.eps)

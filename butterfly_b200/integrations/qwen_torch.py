@@ -428,17 +428,19 @@ class QwenCUDAButterflyAttention(nn.Module):
             raise ValueError(f"compressed Butterfly kernels need head_dim 128, layer has {self.head_dim}")
         return reason, comp_cache, cache_len, k_len_after
 
-    def attend(self, q, k, v, comp_cache, cache_len: int, k_len_after: int, cache_position=None):
+    def attend(self, q, k, v, comp_cache, cache_len: int, k_len_after: int, cache_position=None, qk_prep=None):
         """Compressed attention of q [B,Hq,Tq,dh] over k/v [B,Hkv,Tk,dh] (HF-cache history
         included, or the new tokens only when ``comp_cache`` holds the history).  Returns
-        ([B,Hq,Tq,dh] view of [B,Tq,Hq,dh] storage, backend name, layout-cache hit)."""
+        ([B,Hq,Tq,dh] view of [B,Tq,Hq,dh] storage, backend name, layout-cache hit).
+        ``qk_prep`` (a decode step into ``comp_cache`` only): q / k are raw projection rows and
+        the step applies the q/k norm and rotary embedding itself (see decode_step)."""
         q_len = int(q.shape[2])
         W = int(self.cfg.compressed_local_window_tokens)
         scale = 1.0 / math.sqrt(self.head_dim)  # SDPA's default, as the reference (the module scaling is not passed)
         lay, hit = self._layout(k_len_after)
         if comp_cache is not None:
             if q_len == 1 and cache_len > 0:
-                out = comp_cache.decode_step(q, k, v, lay, scale=scale)
+                out = comp_cache.decode_step(q, k, v, lay, scale=scale, qk_prep=qk_prep)
                 backend = "compressed_cache_decode_step"
             elif cache_len == 0:
                 # The prefill's block means are written straight into the cache's summary

@@ -256,6 +256,22 @@ BNA_API int bna_gemv(const void* x, int64_t x_stride, const void* w, int64_t out
                      const void* res, int64_t res_stride, void* out, int64_t out_stride, int32_t tokens,
                      int32_t dtype, void* stream);
 
+/* The fused decode step with the new token's q/k preparation fused in (replaces
+ * bna_qk_norm_rope + bna_decode_step for one token): q_raw [B,Hq,1,dh] and k_raw
+ * [B,Hkv,1,dh] are the raw projection rows (the query half of a gated q_proj output read in
+ * place); each row gets the Qwen3.5 RMSNorm (q_norm_weight / k_norm_weight [dh], eps) and the
+ * rotary embedding on its first `rot` dims with cos / sin of sequence b at
+ * cos + b * cs_batch_stride, before the append (the ring stores the prepared key) and the
+ * attention.  Reference: bna/integrations/qwen_torch.py:535-573 (q/k norm, RoPE, cache
+ * update) followed by the decode branch :1417-1427. */
+BNA_API int bna_decode_step_qk(const bna_tensor4* q_raw, const bna_tensor4* k_raw, const bna_tensor4* v_new,
+                               bna_tensor4* ring_k, bna_tensor4* ring_v, bna_tensor4* sum_k, bna_tensor4* sum_v,
+                               bna_tensor4* out, float* lse, int64_t lse_stride_b, int64_t lse_stride_h,
+                               int32_t dtype, const bna_route* route, int32_t window, int64_t pos, int64_t ring,
+                               int64_t close_block, int64_t close_slot, int32_t num_summary_limit, float scale,
+                               const void* q_norm_weight, const void* k_norm_weight, const void* cos,
+                               const void* sin, int64_t cs_batch_stride, int32_t rot, float eps, void* stream);
+
 /* ---- Prefill without caller-provided scratch -------------------------------------------
  * No counterpart in the reference.  For callers that cannot allocate device memory
  * (no cudaMalloc inside their host framework's capture/allocator regions, or a fixed

@@ -188,3 +188,40 @@ def test_decode_gemv_kernels_match_eager():
         qg = torch.randn(M, Hq, 2 * dh, device="cuda", generator=g).bfloat16()
         ref = r + F.linear(o.reshape(M, -1) * torch.sigmoid(qg[..., dh:].reshape(M, -1)), Wo)
         _close(glue.gemv_gated(o, qg[..., dh:], Wo, residual=r), ref, 0.9, ulps=2)
+
+
+def test_decode_step_with_fused_qk_prep_equals_separate_kernels():
+    """bna_decode_step_qk (q/k norm + RoPE inside the decode step) gives bit-identical
+    outputs and ring contents to bna_qk_norm_rope followed by bna_decode_step."""
+    from transformers import Qwen3_5TextConfig
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5TextRotaryEmbedding
+
+    import butterfly_b200 as bb
+    from butterfly_b200.cache import CompressedKVCache
+    cfg = Qwen3_5TextConfig(hidden_size=1024, num_attention_heads=8, num_key_value_heads=2, head_dim=128,
+                            num_hidden_layers=1, layer_types=["full_attention"])
+    rope = Qwen3_5TextRotaryEmbedding(cfg).cuda()
+    g = torch.Generator(device="cuda").manual_seed(8)
+    B, Hq, Hkv, dh, T0 = 3, 8, 2, 128, 1000
+    qn, kn = _norm(dh, 31), _norm(dh, 32)
+    caches = [CompressedKVCache(block_size=128, local_window_tokens=64, max_chunk_size=1024) for _ in range(2)]
+    k0 = torch.randn(B, Hkv, T0, dh, device="cuda", generator=g).bfloat16()
+    for c in caches:
+        c.append(k0, k0)
+    for step in range(150):  # across a block close
+        qkv = torch.randn(B, 1, 2 * Hq * dh + 2 * Hkv * dh, device="cuda", generator=g).bfloat16() * 2
+        qg = qkv[..., :2 * Hq * dh].view(B, 1, Hq, 2 * dh)
+        k_raw = qkv[..., 2 * Hq * dh:2 * Hq * dh + Hkv * dh].view(B, 1, Hkv, dh)
+        v = qkv[..., 2 * Hq * dh + Hkv * dh:].view(B, 1, Hkv, dh)
+        pos = T0 + step
+        cos, sin = rope(qkv, torch.full((B, 1), pos, device="cuda"))
+        lay = bb.build_block_butterfly_layout(seq_len=pos + 1, block_size=128, num_key_value_heads=Hkv,
+                                              num_key_value_groups=Hq // Hkv, layer_idx=4, local_window_blocks=1,
+                                              sink_count=1, partner_count=1, partner_rule="causal_shift")
+        q, k = glue.qk_norm_rope(qg[..., :dh], k_raw, qn.weight, kn.weight, cos, sin, qn.eps)
+        a = caches[0].decode_step(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), lay)
+        b = caches[1].decode_step(qg[..., :dh].transpose(1, 2), k_raw.transpose(1, 2), v.transpose(1, 2), lay,
+                                  qk_prep=(qn.weight, kn.weight, cos, sin, qn.eps))
+        assert torch.equal(a, b), step
+    for x, y in zip(caches[0].state, caches[1].state):
+        assert torch.equal(x, y)
