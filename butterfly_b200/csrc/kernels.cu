@@ -6,6 +6,7 @@
 //   * device dump of the prefill selection   attention_wayfinder_permute.py:912-966
 // All use coalesced 128-bit loads, shared-memory staging and warp-shuffle reductions.
 #include <cuda_runtime.h>
+#include <type_traits>
 
 #include "common.cuh"
 #include "route.cuh"
@@ -167,8 +168,10 @@ struct ActiveArgs {
   int host_ids[kMaxSummaries];
 };
 
-// 512 threads (256 for G >= 8, where each warp keeps more per-head state in registers).
-__host__ __device__ constexpr int decode_threads(int G) { return G >= 8 ? 256 : 512; }
+// 128 threads: four warps of 16-key tensor-core tiles (measured faster than 256 / 512,
+// where more warps mean costlier barriers and merges for the few tiles of a window).
+__host__ __device__ constexpr int decode_threads(int G) { return 128; }
+constexpr int kDecPitch = 256 + 16;  // staged row pitch (bytes): spreads ldmatrix / fragment rows over banks
 // floats of the partial-sum region: the per-warp (o) partials, or the block-mean buffer of
 // a fused close (8 floats per thread)
 __host__ __device__ constexpr int decode_part_floats(int G) {
@@ -177,8 +180,9 @@ __host__ __device__ constexpr int decode_part_floats(int G) {
 }
 size_t decode_smem_bytes(int G, int window) {
   const int maxk = window + kMaxSummaries;
-  return (size_t)2 * maxk * 256 + (size_t)G * 256 + sizeof(float) * (size_t)decode_part_floats(G) +
-         sizeof(float) * (size_t)(decode_threads(G) / 32) * G * 2 + sizeof(int) * (1 + kMaxSummaries);
+  return (size_t)2 * kDecPitch * ((maxk + 15) / 16 * 16) + (size_t)G * kDecPitch + sizeof(float) * (size_t)decode_part_floats(G) +
+         sizeof(float) * (size_t)(decode_threads(G) / 32) * G * 2 + sizeof(int) * (1 + kMaxSummaries) +
+         sizeof(float) * (size_t)G * (decode_threads(G) / 32 + 1);
 }
 
 __device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc) {
@@ -188,6 +192,31 @@ __device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// D += A B for one m16n8k16 tile (A row-major 16x16, B column-major 16x8, fp32 accumulate).
+template <typename T>
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+// Four 8x8 16-bit matrices from shared memory, transposed (lanes 8i..8i+7 give the row
+// addresses of matrix i).
+__device__ __forceinline__ void ldmatrix_x4_trans(const void* smem_row, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                                  uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"((uint32_t)__cvta_generic_to_shared(smem_row)));
+}
+
 // One CTA per (query index, b * Hkv) serves the G query heads of a KV head.
 //   1. loads: the raw window rows, the routed summary rows and the G query rows arrive in
 //      shared memory by cp.async in one round trip.  In a fused decode step the ring rows of
@@ -195,11 +224,13 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 //      dependent launch, while the previous kernel of the stream finishes): only the
 //      immediately preceding kernel can still be running, and in a decode step the ring rows
 //      it may write are those of position p - 1 (the previous step's append) at most.
-//   2. one pass per warp: warp w takes keys w, w + NW, ...; for each key the G scores are
-//      warp all-reduced dot products (lane l holds dims 4l..4l+3) and an online softmax
-//      (exp2 domain) keeps each head's running max, sum and 128-wide output in registers.
-//   3. the NW per-warp (max, sum, output) partials of each head are merged once through
-//      shared memory (the online log-sum-exp merge) and written out.
+//   2. one pass per half-warp: the 2 NW half-warps take keys in turn; for each key the G
+//      scores are 16-lane reduced dot products (lane l holds dims 8 (l & 15) .. + 7) and an
+//      online softmax (exp2 domain) keeps each head's running max, sum and output columns
+//      in registers.
+//   3. the 2 NW (max, sum, output) partials of each head are merged once through shared
+//      memory (the online log-sum-exp merge): one thread per head computes the rescale
+//      factors, then one thread per (head, two columns) sums the partials.
 // Optionally the CTA also closes one block into the summary pool and appends the new token
 // to the ring (fused decode step).
 template <typename T, int G>
@@ -207,10 +238,10 @@ __global__ void __launch_bounds__(decode_threads(G)) decode_kernel(const ActiveA
   constexpr int NT = decode_threads(G);
   constexpr int NW = NT / 32;
   extern __shared__ __align__(16) uint8_t dsm_raw[];
-  const int maxk = a.window + kMaxSummaries;
-  uint8_t* kv = dsm_raw;                                      // [2][maxk][256 B] K rows, V rows
-  uint8_t* qraw = kv + 2 * maxk * 256;                        // [G][256 B] queries as loaded
-  float* part = reinterpret_cast<float*>(qraw + G * 256);     // [NW][G][128] partial outputs
+  const int maxk = (a.window + kMaxSummaries + 15) / 16 * 16;  // rows per K / V region (whole 16-key tiles)
+  uint8_t* kv = dsm_raw;                                      // [2][maxk][kDecPitch] K rows, V rows
+  uint8_t* qraw = kv + 2 * maxk * kDecPitch;                  // [G][kDecPitch] queries as loaded
+  float* part = reinterpret_cast<float*>(qraw + G * kDecPitch);  // [NW][G][128] partial outputs
   float* red = part;                                          // block-mean buffer of a fused close
   float* ml = part + decode_part_floats(G);                   // [NW][G][2] partial max, sum
   int* sel = reinterpret_cast<int*>(ml + NW * G * 2);         // [1 + 16] summary count + ids
@@ -238,7 +269,7 @@ __global__ void __launch_bounds__(decode_threads(G)) decode_kernel(const ActiveA
         if (a.ring > 0 && idx >= (int)a.ring) idx -= (int)a.ring;
         src = row_ptr(isv ? a.v : a.k, b, kvh, idx);
       }
-      cp_async_16(kv + (isv * maxk + j) * 256 + ch * 16, src + ch * 16);
+      cp_async_16(kv + (isv * maxk + j) * kDecPitch + ch * 16, src + ch * 16);
     }
   };
   // raw window [lo, hi]; with a fused append the newest row (p) is read from the input
@@ -276,13 +307,13 @@ __global__ void __launch_bounds__(decode_threads(G)) decode_kernel(const ActiveA
       const int isv = c >= a.host_ns * 16;
       const int e = isv ? c - a.host_ns * 16 : c;
       const int j = e >> 4, ch = e & 15;
-      cp_async_16(kv + (isv * maxk + nraw + j) * 256 + ch * 16,
+      cp_async_16(kv + (isv * maxk + nraw + j) * kDecPitch + ch * 16,
                   row_ptr(isv ? a.vs : a.ks, b, kvh, a.host_ids[j]) + ch * 16);
     }
   }
   for (int c = threadIdx.x; c < G * 16; c += NT) {
     const int g = c >> 4, ch = c & 15;
-    cp_async_16(qraw + g * 256 + ch * 16, row_ptr(a.q, b, kvh * G + g, t) + ch * 16);
+    cp_async_16(qraw + g * kDecPitch + ch * 16, row_ptr(a.q, b, kvh * G + g, t) + ch * 16);
   }
   if (a.close_block >= 0) {  // fused block close: mean of the block's tokens from the ring
     const int BS = a.route.block_size;
@@ -307,7 +338,7 @@ __global__ void __launch_bounds__(decode_threads(G)) decode_kernel(const ActiveA
     const int isv = c >= ns * 16;
     const int e = isv ? c - ns * 16 : c;
     const int j = e >> 4, ch = e & 15;
-    cp_async_16(kv + (isv * maxk + nraw + j) * 256 + ch * 16, row_ptr(isv ? a.vs : a.ks, b, kvh, sel[1 + j]) + ch * 16);
+    cp_async_16(kv + (isv * maxk + nraw + j) * kDecPitch + ch * 16, row_ptr(isv ? a.vs : a.ks, b, kvh, sel[1 + j]) + ch * 16);
   }
   cp_async_wait_all();
   __syncthreads();
@@ -315,7 +346,7 @@ __global__ void __launch_bounds__(decode_threads(G)) decode_kernel(const ActiveA
     // warp r normalises and rotates query row r (r < G) or, for r == G, the new key row
 #pragma unroll 1
     for (int r = warp; r <= G; r += NW) {
-      uint8_t* row = r < G ? qraw + r * 256 : kv + (nraw - 1) * 256;
+      uint8_t* row = r < G ? qraw + r * kDecPitch : kv + (nraw - 1) * kDecPitch;
       const uint8_t* wp = static_cast<const uint8_t*>(r < G ? a.qn_w : a.kn_w);
       const uint2 u = *reinterpret_cast<const uint2*>(row + 8 * lane);
       const uint2 uw = *reinterpret_cast<const uint2*>(wp + 8 * lane);
@@ -346,82 +377,159 @@ __global__ void __launch_bounds__(decode_threads(G)) decode_kernel(const ActiveA
     const int isv = threadIdx.x >= 16;
     const int ch = threadIdx.x & 15;
     st_128(row_ptr(isv ? a.v : a.k, b, kvh, slot) + ch * 16,
-           *reinterpret_cast<const uint4*>(kv + (isv * maxk + nraw - 1) * 256 + ch * 16));
+           *reinterpret_cast<const uint4*>(kv + (isv * maxk + nraw - 1) * kDecPitch + ch * 16));
   }
 
-  // one pass per warp over its keys: scores, online softmax and weighted values
-  float qf[G][4];
+  // Tensor-core tiles (mma.sync m16n8k16, fp32 accumulate): warp w takes the 16-key tiles
+  // w, w + NW, ... of the staged keys.  S = Q K^T for its tile has the G heads as rows (padded
+  // to 16) and 16 keys as columns; an online softmax (exp2 domain) per head turns it into P
+  // (16-bit, in registers, already in the A-operand layout), and O += P V over the 128 value
+  // columns (16 n-tiles, V fragments by ldmatrix.trans).  Rows >= G and keys >= nk are masked.
+  const int gid = lane >> 2, tig = lane & 3;
+  // rows nk .. end of the last tile: zero V so that P = 0 there never meets stale bits
+  for (int c = threadIdx.x; c < ((nk + 15) / 16 * 16 - nk) * 16; c += NT)
+    *reinterpret_cast<uint4*>(kv + (maxk + nk + (c >> 4)) * kDecPitch + (c & 15) * 16) = make_uint4(0, 0, 0, 0);
+  __syncthreads();
+  uint32_t qa[8][4];  // Q fragments for the 8 k-steps of 16 head dims (rows gid, gid + 8)
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const uint2 u = *reinterpret_cast<const uint2*>(qraw + g * 256 + 8 * lane);
-    const float2 f0 = ElemTraits<T>::unpack2(u.x), f1 = ElemTraits<T>::unpack2(u.y);
-    qf[g][0] = f0.x * a.scale_log2;
-    qf[g][1] = f0.y * a.scale_log2;
-    qf[g][2] = f1.x * a.scale_log2;
-    qf[g][3] = f1.y * a.scale_log2;
+  for (int kk = 0; kk < 8; ++kk) {
+    const int d = kk * 16 + tig * 2;
+    qa[kk][0] = gid < G ? *reinterpret_cast<const uint32_t*>(qraw + gid * kDecPitch + 2 * d) : 0u;
+    qa[kk][1] = gid + 8 < G ? *reinterpret_cast<const uint32_t*>(qraw + (gid + 8) * kDecPitch + 2 * d) : 0u;
+    qa[kk][2] = gid < G ? *reinterpret_cast<const uint32_t*>(qraw + gid * kDecPitch + 2 * (d + 8)) : 0u;
+    qa[kk][3] = gid + 8 < G ? *reinterpret_cast<const uint32_t*>(qraw + (gid + 8) * kDecPitch + 2 * (d + 8)) : 0u;
   }
-  float m[G], l[G], o[G][4];
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};  // rows gid, gid + 8
+  float acc[16][4];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
-    o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
-  }
+  for (int n = 0; n < 16; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+  const int ntiles = (nk + 15) >> 4;
 #pragma unroll 1
-  for (int j = warp; j < nk; j += NW) {
-    const uint2 uk = *reinterpret_cast<const uint2*>(kv + j * 256 + 8 * lane);
-    const uint2 uv = *reinterpret_cast<const uint2*>(kv + (maxk + j) * 256 + 8 * lane);
-    const float2 k0 = ElemTraits<T>::unpack2(uk.x), k1 = ElemTraits<T>::unpack2(uk.y);
-    const float2 v0 = ElemTraits<T>::unpack2(uv.x), v1 = ElemTraits<T>::unpack2(uv.y);
-    float s[G];
+  for (int kt = warp; kt < ntiles; kt += NW) {
+    const int k0 = kt * 16;
+    float sacc[2][4];  // two 8-key n-tiles
 #pragma unroll
-    for (int g = 0; g < G; ++g) s[g] = fmaf(qf[g][0], k0.x, fmaf(qf[g][1], k0.y, fmaf(qf[g][2], k1.x, qf[g][3] * k1.y)));
+    for (int h = 0; h < 2; ++h) {
+      sacc[h][0] = sacc[h][1] = sacc[h][2] = sacc[h][3] = 0.f;
+      const uint8_t* krow = kv + (k0 + h * 8 + gid) * kDecPitch;
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1)
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + 2 * (kk * 16 + tig * 2));
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + 2 * (kk * 16 + tig * 2 + 8));
+        mma_16816<T>(sacc[h], qa[kk], b0, b1);
+      }
+    }
+    // scale, mask keys >= nk, tile max per row
+    float tmax[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-      for (int g = 0; g < G; ++g) s[g] += __shfl_xor_sync(0xffffffffu, s[g], off);
+    for (int h = 0; h < 2; ++h)
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float mn = fmaxf(m[g], s[g]);
-      const float c = exp2f(m[g] - mn);  // 0 on the first key (m = -inf)
-      const float pw = exp2f(s[g] - mn);
-      l[g] = fmaf(l[g], c, pw);
-      o[g][0] = fmaf(o[g][0], c, pw * v0.x);
-      o[g][1] = fmaf(o[g][1], c, pw * v0.y);
-      o[g][2] = fmaf(o[g][2], c, pw * v1.x);
-      o[g][3] = fmaf(o[g][3], c, pw * v1.y);
-      m[g] = mn;
+      for (int e = 0; e < 4; ++e) {
+        const int key = k0 + h * 8 + tig * 2 + (e & 1);
+        const float v = key < nk ? sacc[h][e] * a.scale_log2 : -INFINITY;
+        sacc[h][e] = v;
+        tmax[e >> 1] = fmaxf(tmax[e >> 1], v);
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      tmax[r] = fmaxf(tmax[r], __shfl_xor_sync(0xffffffffu, tmax[r], 1));
+      tmax[r] = fmaxf(tmax[r], __shfl_xor_sync(0xffffffffu, tmax[r], 2));
+    }
+    float corr[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const float mn = fmaxf(mrow[r], tmax[r]);
+      corr[r] = ex2_approx(mrow[r] - mn);  // 0 when the row had no keys yet
+      mrow[r] = mn;
+      lrow[r] *= corr[r];
+    }
+    uint32_t pa[4];
+    float psum[2] = {0.f, 0.f};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float p0 = ex2_approx(sacc[h][0] - mrow[0]), p1 = ex2_approx(sacc[h][1] - mrow[0]);
+      const float p2 = ex2_approx(sacc[h][2] - mrow[1]), p3 = ex2_approx(sacc[h][3] - mrow[1]);
+      psum[0] += p0 + p1;
+      psum[1] += p2 + p3;
+      pa[h * 2] = ElemTraits<T>::pack2(p0, p1);      // row gid, keys 8h + 2 tig ..
+      pa[h * 2 + 1] = ElemTraits<T>::pack2(p2, p3);  // row gid + 8
+    }
+    // A fragment order: (row gid, k 0-7), (row gid+8, k 0-7), (row gid, k 8-15), (row gid+8, k 8-15)
+    const uint32_t pfrag[4] = {pa[0], pa[1], pa[2], pa[3]};
+#pragma unroll
+    for (int r = 0; r < 2; ++r) lrow[r] += psum[r];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      acc[n][0] *= corr[0];
+      acc[n][1] *= corr[0];
+      acc[n][2] *= corr[1];
+      acc[n][3] *= corr[1];
+    }
+    // V fragments: ldmatrix.x4.trans over (keys k0..k0+15) x (columns 16 np .. 16 np + 15)
+    const uint8_t* vbase = kv + (size_t)maxk * kDecPitch;
+#pragma unroll
+    for (int np = 0; np < 8; ++np) {
+      const int mat = lane >> 3, rr = lane & 7;
+      const uint8_t* addr = vbase + (k0 + (mat & 1) * 8 + rr) * kDecPitch + 2 * (np * 16 + (mat >> 1) * 8);
+      uint32_t v0, v1, v2, v3;
+      ldmatrix_x4_trans(addr, v0, v1, v2, v3);
+      mma_16816<T>(acc[2 * np], pfrag, v0, v1);
+      mma_16816<T>(acc[2 * np + 1], pfrag, v2, v3);
     }
   }
+  // row sums across the quad
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    *reinterpret_cast<float4*>(part + (warp * G + g) * 128 + 4 * lane) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
-    if (lane == 0) {
-      ml[(warp * G + g) * 2] = m[g];
-      ml[(warp * G + g) * 2 + 1] = l[g];
+  for (int r = 0; r < 2; ++r) {
+    lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
+    lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
+  }
+  // partials of warp w: outputs at part[w][g][col], (max, sum) at ml[w][g]
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int g = gid + 8 * r;
+    if (g < G) {
+#pragma unroll
+      for (int n = 0; n < 16; ++n)
+        *reinterpret_cast<float2*>(part + (warp * G + g) * 128 + n * 8 + tig * 2) = make_float2(acc[n][2 * r], acc[n][2 * r + 1]);
+      if (tig == 0) {
+        ml[(warp * G + g) * 2] = mrow[r];
+        ml[(warp * G + g) * 2 + 1] = lrow[r];
+      }
     }
   }
   __syncthreads();
-  // merge the warps' partials per head: thread = (head, two columns)
+  // per head: the global max, each partial's rescale factor and the total sum, once
+  constexpr int NP = NW;  // partials per head
+  float* coef = reinterpret_cast<float*>(sel + 1 + kMaxSummaries);  // [G][NP + 1]
+  const int nact = ntiles < NW ? ntiles : NW;  // warps that saw keys
+  if (threadIdx.x < G) {
+    const int g = threadIdx.x;
+    float M = -INFINITY;
+    for (int w = 0; w < nact; ++w) M = fmaxf(M, ml[(w * G + g) * 2]);
+    float L = 0.f;
+    for (int w = 0; w < nact; ++w) {
+      const float mw = ml[(w * G + g) * 2];
+      const float cw = mw == -INFINITY ? 0.f : ex2_approx(mw - M);
+      coef[g * (NP + 1) + w] = cw;
+      L = fmaf(ml[(w * G + g) * 2 + 1], cw, L);
+    }
+    coef[g * (NP + 1) + NP] = L > 0.f ? 1.f / L : 0.f;
+    if (a.lse) a.lse[b * a.ls_b + (int64_t)(kvh * G + g) * a.ls_h + t] = (M + log2f(L)) * 0.6931471805599453f;
+  }
+  __syncthreads();
+  // merge: thread = (head, two columns)
 #pragma unroll 1
   for (int r = threadIdx.x; r < G * 64; r += NT) {
     const int g = r >> 6, c = (r & 63) * 2;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) M = fmaxf(M, ml[(w * G + g) * 2]);
-    float L = 0.f, s0 = 0.f, s1 = 0.f;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) {
-      const float mw = ml[(w * G + g) * 2];
-      const float cw = mw == -INFINITY ? 0.f : exp2f(mw - M);
-      L = fmaf(ml[(w * G + g) * 2 + 1], cw, L);
+    const float* cf = coef + g * (NP + 1);
+    float s0 = 0.f, s1 = 0.f;
+    for (int w = 0; w < nact; ++w) {
       const float2 f = *reinterpret_cast<const float2*>(part + (w * G + g) * 128 + c);
-      s0 = fmaf(f.x, cw, s0);
-      s1 = fmaf(f.y, cw, s1);
+      s0 = fmaf(f.x, cf[w], s0);
+      s1 = fmaf(f.y, cf[w], s1);
     }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
+    const float inv = cf[NP];
     *reinterpret_cast<uint32_t*>(row_ptr(a.out, b, kvh * G + g, t) + c * 2) = ElemTraits<T>::pack2(s0 * inv, s1 * inv);
-    if (c == 0 && a.lse) a.lse[b * a.ls_b + (int64_t)(kvh * G + g) * a.ls_h + t] = (M + log2f(L)) * 0.6931471805599453f;
   }
 }
 
