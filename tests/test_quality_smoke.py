@@ -47,6 +47,6 @@ def test_quality_smoke_runs_stock_and_compressed():
     res = quality_smoke(m, prompt_ids(1000, 4096).cuda(), decode_len=8, top_k=50)
     met = res["metrics"]
     assert met["top_k_total"] == 50 and 0 <= met["top_k_overlap"] <= 50
-    assert math.isfinite(met["kl_stock_compressed"]) and met["kl_stock_compressed"] >= -1e-6
+    assert math.isfinite(met["kl_stock_compressed"]) and math.isfinite(met["kl_compressed_stock"])
     assert len(res["stock"]["decoded_ids"]) == 8 and len(res["compressed"]["decoded_ids"]) == 8
     assert not list(qt.iter_qwen_butterfly_layers(m))  # stock attention restored
