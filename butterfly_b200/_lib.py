@@ -23,7 +23,7 @@ EXPORTED = (
     "bna_prefill_selection_device", "bna_compress_blocks", "bna_compress_kv_blocks", "bna_prefill_attention",
     "bna_active_attention", "bna_cache_append", "bna_decode_step", "bna_prefill_attention_static_scratch",
     "bna_rmsnorm", "bna_qk_norm_rope", "bna_gate_sigmoid_mul", "bna_swiglu", "bna_gemv_rmsnorm", "bna_gemv_gated",
-    "bna_gemv", "bna_launch_probe", "bna_decode_step_qk", "bna_decode_layer_tail",
+    "bna_gemv", "bna_launch_probe", "bna_decode_step_qk",
 )
 
 
@@ -81,8 +81,6 @@ def lib() -> ctypes.CDLL:
             "bna_gemv_rmsnorm": (i32, [vp, i64, vp, i64, vp, f32, vp, i64, vp, i64, i64, i32, vp, i64, i32, i32, vp]),
             "bna_gemv_gated": (i32, [vp, vp, i64, i64, i32, vp, i64, i64, vp, i64, vp, i64, i32, i32, vp]),
             "bna_launch_probe": (i32, [i32, vp]),
-            "bna_decode_layer_tail": (i32, [vp, vp, i64, i64, i32, i32, vp, vp, vp, f32, vp, vp, i32, i32, vp, f32, vp, i32,
-                                            vp, vp, vp, vp, i32, i32, vp]),
             "bna_decode_step_qk": (i32, [T4, T4, T4, T4, T4, T4, T4, T4, vp, i64, i64, i32, R, i32, i64, i64, i64, i64, i32,
                                          f32, vp, vp, vp, vp, i64, i32, f32, vp]),
             "bna_gemv": (i32, [vp, i64, vp, i64, i64, vp, i64, vp, i64, i32, i32, vp]),

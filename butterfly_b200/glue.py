@@ -213,33 +213,3 @@ def gemv(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = No
                                    _lib.dtype_code(x.dtype), _lib.stream_ptr(x.device)))
     return out
 
-
-def decode_layer_tail(o: torch.Tensor, gate: torch.Tensor, x: torch.Tensor, w_o: torch.Tensor,
-                      post_norm_weight: torch.Tensor, post_eps: float, w_gate_up: torch.Tensor, w_down: torch.Tensor,
-                      next_norm_weight: Optional[torch.Tensor] = None, next_eps: float = 0.0,
-                      w_qkv: Optional[torch.Tensor] = None):
-    """The decoder layer after its attention for one decode step (M <= 8 tokens), one
-    cooperative launch: returns (x3 [M,H], qkv [M, qkv_rows] of the next layer or None).
-    o [M,Hq,dh] contiguous; gate [M,Hq,dh] with a contiguous head_dim; x [M,H]."""
-    _lib.require_cuda(o, gate, x, w_o, w_gate_up, w_down)
-    M, Hq, dh = o.shape
-    H = int(x.shape[1])
-    inter = int(w_down.shape[1])
-    if not o.is_contiguous() or not x.is_contiguous() or gate.stride(-1) != 1:
-        raise ValueError("decode_layer_tail: o and x must be contiguous, gate's head_dim contiguous")
-    for w in (w_o, w_gate_up, w_down, post_norm_weight) + ((w_qkv, next_norm_weight) if w_qkv is not None else ()):
-        if not w.is_contiguous() or w.dtype != x.dtype:
-            raise ValueError("decode_layer_tail: weights must be contiguous and of x's dtype")
-    x2 = torch.empty((M, H), device=x.device, dtype=x.dtype)
-    act = torch.empty((M, inter), device=x.device, dtype=x.dtype)
-    x3 = torch.empty((M, H), device=x.device, dtype=x.dtype)
-    nq = int(w_qkv.shape[0]) if w_qkv is not None else 0
-    qkv = torch.empty((M, nq), device=x.device, dtype=x.dtype) if w_qkv is not None else None
-    gts = gate.stride(0) if M > 1 else Hq * gate.stride(1)
-    _lib.check(_lib.lib().bna_decode_layer_tail(
-        o.data_ptr(), gate.data_ptr(), gts, gate.stride(1), Hq, dh, x.data_ptr(), w_o.data_ptr(),
-        post_norm_weight.data_ptr(), float(post_eps), w_gate_up.data_ptr(), w_down.data_ptr(), H, inter,
-        next_norm_weight.data_ptr() if w_qkv is not None else None, float(next_eps),
-        w_qkv.data_ptr() if w_qkv is not None else None, nq, x2.data_ptr(), act.data_ptr(), x3.data_ptr(),
-        qkv.data_ptr() if qkv is not None else None, M, _lib.dtype_code(x.dtype), _lib.stream_ptr(x.device)))
-    return x3, qkv

@@ -16,12 +16,11 @@ rotary-embedding concatenations, separate sigmoid / SiLU / multiply / residual p
     gu  = h2 @ [Wg; Wu]^T                             one GEMM     (gate/up merged)
     x2 += swiglu(gu) @ Wd^T                           one kernel + one GEMM accumulating into x2
 
-For a decode step (one token per sequence, up to 8 sequences) into a two-pool cache a layer
-is two launches: the cache decode step with the new token's q/k norm + RoPE fused in, and
-one cooperative kernel for everything after the attention (gate + o_proj + residual,
-rmsnorm + gate/up + SwiGLU, down_proj + residual, and the NEXT layer's rmsnorm + q/k/v
-projections, handed to that layer), its phases separated by grid barriers.  Other decode
-steps use weight-streaming GEMV kernels with the same fusions, one launch per projection.
+For a decode step (one token per sequence, up to 8 sequences) the projections are instead
+weight-streaming GEMV kernels with the neighbouring steps fused in: rmsnorm+qkv,
+gate+o_proj+residual, rmsnorm+gate/up+SwiGLU, down_proj+residual, and (into a two-pool
+cache) the decode step with the q/k norm + RoPE of the new token fused in: five launches
+per layer, each overlapping the previous one's tail through programmatic dependent launch.
 
 The projection weights are moved into one buffer per layer ([Wq; Wk; Wv] and [Wg; Wu]) and
 the modules' ``weight`` parameters become views of it, so the model's parameters, its
@@ -75,8 +74,6 @@ class _FusedState:
         self.w_gu = _merge_weights([mlp.gate_proj, mlp.up_proj])
         self.hq, self.hkv, self.dh = attn.num_heads, attn.num_key_value_heads, attn.head_dim
         self.inter = mlp.gate_proj.out_features
-        self.next_layer: Optional[nn.Module] = None  # the following fused decoder layer
-        self.pending_qkv = None  # (position, [B, rows]) projections computed by the previous layer's tail
 
 
 def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=None, attention_mask=None,
@@ -95,11 +92,7 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
     hq, hkv, dh = st.hq, st.hkv, st.dh
     x = hidden_states
     decode = T == 1 and B <= 8 and H % 256 == 0 and st.inter % 256 == 0 and attn._shard is None
-    pend, st.pending_qkv = st.pending_qkv, None
-    if decode and pend is not None and comp_cache is not None and pend[0] == comp_cache.offset \
-            and pend[1].shape[0] == B:
-        qkv = pend[1].view(B, 1, -1)  # computed by the previous layer's tail kernel
-    elif decode:  # weight-streaming projections with the norms, gate and residual adds fused in
+    if decode:  # weight-streaming projections with the norms, gate and residual adds fused in
         qkv = glue.gemv_rmsnorm(x.view(B, H), self.input_layernorm.weight, self.input_layernorm.eps,
                                 st.w_qkv).view(B, 1, -1)
     else:
@@ -131,21 +124,6 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
         if comp_cache is None and past_key_values is not None:
             kt, vt = past_key_values.update(kt, vt, attn.layer_idx)
         out, backend, hit = attn.attend(qt, kt, vt, comp_cache, cache_len, k_len_after, kwargs.get("cache_position"))
-    if decode and DECODE_TAIL and comp_cache is not None:
-        # the rest of this layer and the next layer's projections: one cooperative launch
-        nxt = st.next_layer
-        ns = getattr(nxt, "_bna_fused", None) if nxt is not None else None
-        if ns is not None and ns.attn._shard is not None:
-            ns = None
-        x3, qkv_next = glue.decode_layer_tail(
-            out.transpose(1, 2).reshape(B, hq, dh), qg[:, 0, :, dh:], x.view(B, H), src.o_proj.weight,
-            self.post_attention_layernorm.weight, self.post_attention_layernorm.eps, st.w_gu,
-            self.mlp.down_proj.weight, nxt.input_layernorm.weight if ns is not None else None,
-            nxt.input_layernorm.eps if ns is not None else 0.0, ns.w_qkv if ns is not None else None)
-        if ns is not None:
-            ns.pending_qkv = (comp_cache.offset - 1, qkv_next)
-        attn._profile(T, k_len_after, backend, hit, t0, fused=True)
-        return x3.view(B, 1, H)
     if decode:
         x2 = glue.gemv_gated(out.transpose(1, 2).reshape(B, hq, dh), qg[:, 0, :, dh:], src.o_proj.weight,
                              residual=x.view(B, H))
@@ -163,11 +141,6 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
     x2.view(-1, H).addmm_(act.view(-1, st.inter), self.mlp.down_proj.weight.t())
     attn._profile(T, k_len_after, backend, hit, t0, fused=True)
     return x2
-
-
-# Decode steps into a two-pool cache run each layer after its attention as one cooperative
-# kernel (bna_decode_layer_tail), which also computes the next layer's q/k/v projections.
-DECODE_TAIL = True
 
 
 def _fused_norm_forward(self, x: torch.Tensor):
@@ -195,10 +168,6 @@ def fuse_qwen_decoder_layers(model: nn.Module) -> list[int]:
         layer._bna_fused = _FusedState(layer)
         layer.forward = types.MethodType(_fused_layer_forward, layer)
         fused.append(idx)
-    for i in range(len(decoder.layers) - 1):  # link consecutive fused layers (decode tail hand-off)
-        a, b = decoder.layers[i], decoder.layers[i + 1]
-        if hasattr(a, "_bna_fused"):
-            a._bna_fused.next_layer = b if hasattr(b, "_bna_fused") else None
     norm = getattr(decoder, "norm", None)
     if fused and norm is not None and _is_qwen35_norm(norm) and "forward" not in norm.__dict__:
         norm.forward = types.MethodType(_fused_norm_forward, norm)

@@ -272,28 +272,6 @@ BNA_API int bna_decode_step_qk(const bna_tensor4* q_raw, const bna_tensor4* k_ra
                                const void* q_norm_weight, const void* k_norm_weight, const void* cos,
                                const void* sin, int64_t cs_batch_stride, int32_t rot, float eps, void* stream);
 
-/* Everything of a decoder layer's decode step after its attention, for 1..8 tokens, as one
- * cooperative kernel (one CTA per SM, grid barriers between the phases):
- *   x2  = x + W_o (o * sigmoid(gate))                         (written to x2)
- *   act = silu(W_gate h) * W_up h,  h = rmsnorm(x2, post_norm_weight, post_eps)   (act)
- *   x3  = x2 + W_down act                                      (x3: the layer output)
- *   qkv = W_qkv rmsnorm(x3, next_norm_weight, next_eps)        (qkv, only when w_qkv != NULL:
- *                                                               the next layer's projections)
- * o [tokens, heads*head_dim] contiguous; gate[m, h, d] at gate + m*gate_tok_stride +
- * h*gate_head_stride + d; x [tokens, hidden]; W_o [hidden, heads*head_dim]; w_gate_up
- * [2*intermediate, hidden] (gate rows then up rows); w_down [hidden, intermediate]; w_qkv
- * [qkv_rows, hidden].  Same arithmetic as bna_gemv_gated + bna_gemv_rmsnorm(swiglu) +
- * bna_gemv (+ bna_gemv_rmsnorm).  Calls on one device must not overlap (the grid barrier
- * words are shared).  Replaces the eager ops of transformers' Qwen3_5DecoderLayer after the
- * attention (reference bna/integrations/qwen_torch.py:1585-1591 for the gate and o_proj). */
-BNA_API int bna_decode_layer_tail(const void* o, const void* gate, int64_t gate_tok_stride, int64_t gate_head_stride,
-                                  int32_t heads, int32_t head_dim, const void* x, const void* w_o,
-                                  const void* post_norm_weight, float post_eps, const void* w_gate_up,
-                                  const void* w_down, int32_t hidden, int32_t intermediate,
-                                  const void* next_norm_weight, float next_eps, const void* w_qkv, int32_t qkv_rows,
-                                  void* x2, void* act, void* x3, void* qkv, int32_t tokens, int32_t dtype,
-                                  void* stream);
-
 /* ---- Prefill without caller-provided scratch -------------------------------------------
  * No counterpart in the reference.  For callers that cannot allocate device memory
  * (no cudaMalloc inside their host framework's capture/allocator regions, or a fixed

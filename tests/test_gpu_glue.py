@@ -226,29 +226,3 @@ def test_decode_step_with_fused_qk_prep_equals_separate_kernels():
     for x, y in zip(caches[0].state, caches[1].state):
         assert torch.equal(x, y)
 
-
-@pytest.mark.parametrize("M", [1, 3])
-def test_decode_layer_tail_equals_gemv_chain(M):
-    """The cooperative layer-tail kernel computes exactly (bitwise) what the separate decode
-    GEMV kernels compute: gate+o_proj+residual, rmsnorm+gate/up+SwiGLU, down+residual and
-    the next layer's rmsnorm+q/k/v."""
-    g = torch.Generator(device="cuda").manual_seed(14)
-    H, I, Hq, dh, NQ = 1024, 3584, 8, 128, 2560
-    post, nxt = _norm(H, 41), _norm(H, 42)
-    Wo = (torch.randn(H, Hq * dh, device="cuda", generator=g) * 0.03).bfloat16()
-    Wgu = (torch.randn(2 * I, H, device="cuda", generator=g) * 0.03).bfloat16()
-    Wd = (torch.randn(H, I, device="cuda", generator=g) * 0.02).bfloat16()
-    Wq = (torch.randn(NQ, H, device="cuda", generator=g) * 0.03).bfloat16()
-    for _ in range(2):  # twice: the barrier words carry over between launches
-        x = torch.randn(M, H, device="cuda", generator=g).bfloat16()
-        o = torch.randn(M, Hq, dh, device="cuda", generator=g).bfloat16()
-        qg = torch.randn(M, Hq, 2 * dh, device="cuda", generator=g).bfloat16()
-        x2 = glue.gemv_gated(o, qg[..., dh:], Wo, residual=x)
-        act = glue.gemv_rmsnorm(x2, post.weight, post.eps, Wgu, swiglu=True)
-        x3 = glue.gemv(act, Wd, residual=x2)
-        qkv = glue.gemv_rmsnorm(x3, nxt.weight, nxt.eps, Wq)
-        t3, tq = glue.decode_layer_tail(o, qg[..., dh:], x, Wo, post.weight, post.eps, Wgu, Wd, nxt.weight, nxt.eps,
-                                        Wq)
-        u3, uq = glue.decode_layer_tail(o, qg[..., dh:], x, Wo, post.weight, post.eps, Wgu, Wd)
-        torch.cuda.synchronize()
-        assert torch.equal(t3, x3) and torch.equal(tq, qkv) and torch.equal(u3, x3) and uq is None
