@@ -51,8 +51,28 @@ __device__ __forceinline__ void block_mean(const View4& src, int b, int h, int64
   // cache index of first_pos (one modulo); rows step from it with a wrap
   const int64_t idx0 = ring > 0 ? first_pos % ring : first_pos - pos_base;
   if (tl < lanes) {
-#pragma unroll 8
-    for (int j = tl; j < count; j += lanes) {
+    int j = tl;
+    // batches of 8 rows per thread: all eight 128-bit loads are issued before any add
+    for (; j + 7 * lanes < count; j += 8 * lanes) {
+      uint4 u[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        int64_t idx = idx0 + j + r * lanes;
+        if (ring > 0 && idx >= ring) idx -= ring;
+        u[r] = ld_nc_128(row_ptr(src, b, h, idx) + ch * 16);
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const uint32_t w[4] = {u[r].x, u[r].y, u[r].z, u[r].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = ElemTraits<T>::unpack2(w[e]);
+          acc[2 * e] += f.x;
+          acc[2 * e + 1] += f.y;
+        }
+      }
+    }
+    for (; j < count; j += lanes) {
       int64_t idx = idx0 + j;
       if (ring > 0 && idx >= ring) idx -= ring;
       const uint4 u = ld_nc_128(row_ptr(src, b, h, idx) + ch * 16);
@@ -65,7 +85,7 @@ __device__ __forceinline__ void block_mean(const View4& src, int b, int h, int64
       }
     }
   }
-  __syncthreads();
+  __syncthreads();  // red may still be read by a previous call's final sums
   if (tl < lanes) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) red[tl * dh + ch * 8 + e] = acc[e];
