@@ -120,43 +120,84 @@ __device__ __forceinline__ void unpack4(const uint2& u, float (&f)[4], bool bf) 
   f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
 }
 
-// One warp per token: every head row of the token (lane l holds dims 4l..4l+3), all loads
-// of the token issued before any arithmetic.
+// One 128-dim head row held by a half-warp (lane l of the half: dims 8l..8l+7): the
+// Qwen3.5 RMSNorm and the rotate-half rotary embedding on the first 16 * half_lanes dims,
+// with the same arithmetic as qk_row (the 16-lane reductions only differ in order).
+template <typename T>
+__device__ __forceinline__ void qk_row16(float (&x)[8], const float (&w)[8], float eps, int hl, int half_lanes,
+                                         const float (&c)[8], const float (&s)[8]) {
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) ss += x[e] * x[e];
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss * (1.f / 128.f) + eps);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) x[e] = round_to<T>((x[e] * r) * (1.f + w[e]));
+  const bool in_rot = hl < 2 * half_lanes;
+  const bool first = hl < half_lanes;
+  const int lane = threadIdx.x & 31;
+  const int src = in_rot ? (first ? lane + half_lanes : lane - half_lanes) : lane;
+  float p[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) p[e] = __shfl_sync(0xffffffffu, x[e], src);
+  if (in_rot) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float rh = first ? -p[e] : p[e];
+      x[e] = round_to<T>(round_to<T>(x[e] * c[e]) + round_to<T>(rh * s[e]));
+    }
+  }
+}
+
+// One warp per token: its head rows two at a time (one per half-warp, 16-byte loads), all
+// of the token's loads issued before any arithmetic.  Needs rot % 16 == 0.
 template <typename T, int HQ, int HKV>
 __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_kernel(const QKArgs a) {
   constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
-  const int lane = threadIdx.x & 31;
+  constexpr int NH = HQ + HKV;
+  constexpr int NP = (NH + 1) / 2;  // row pairs
+  const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
   const int64_t t = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
   if (t >= a.tokens) return;
-  uint2 raw[HQ + HKV];
+  uint4 raw[NP];
 #pragma unroll
-  for (int h = 0; h < HQ; ++h) raw[h] = *reinterpret_cast<const uint2*>(a.q + 2 * (t * a.q_tok + (int64_t)h * a.q_head) + 8 * lane);
-#pragma unroll
-  for (int h = 0; h < HKV; ++h)
-    raw[HQ + h] = *reinterpret_cast<const uint2*>(a.k + 2 * (t * a.k_tok + (int64_t)h * a.k_head) + 8 * lane);
-  const int half_lanes = a.rot >> 3;  // lanes per half of the rotary dims
-  float c[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
-  if (lane < 2 * half_lanes) {
-    unpack4(*reinterpret_cast<const uint2*>(a.cos + 2 * (t * a.cs_tok) + 8 * lane), c, bf);
-    unpack4(*reinterpret_cast<const uint2*>(a.sin + 2 * (t * a.cs_tok) + 8 * lane), sn, bf);
+  for (int pr = 0; pr < NP; ++pr) {
+    int h = 2 * pr + half;
+    if (h >= NH) h = NH - 1;  // odd row count: the second half repeats the last row (not stored)
+    const uint8_t* src = h < HQ ? a.q + 2 * (t * a.q_tok + (int64_t)h * a.q_head)
+                                : a.k + 2 * (t * a.k_tok + (int64_t)(h - HQ) * a.k_head);
+    raw[pr] = *reinterpret_cast<const uint4*>(src + 16 * hl);
   }
-  float wq[4], wk[4];
-  unpack4(*reinterpret_cast<const uint2*>(a.qw + 8 * lane), wq, bf);
-  if (HKV) unpack4(*reinterpret_cast<const uint2*>(a.kw + 8 * lane), wk, bf);
+  const int half_lanes = a.rot >> 4;
+  float c[8], sn[8], wq[8], wk[8];
 #pragma unroll
-  for (int h = 0; h < HQ + HKV; ++h) {
-    float x[4];
-    unpack4(raw[h], x, bf);
-    qk_row<T>(x, h < HQ ? wq : wk, a.eps, lane, half_lanes, c, sn);
-    uint8_t* dst = h < HQ ? a.q_out + 2 * ((t * HQ + h) * 128) : a.k_out + 2 * ((t * HKV + (h - HQ)) * 128);
-    *reinterpret_cast<uint2*>(dst + 8 * lane) = make_uint2(ElemTraits<T>::pack2(x[0], x[1]),
-                                                           ElemTraits<T>::pack2(x[2], x[3]));
+  for (int e = 0; e < 8; ++e) { c[e] = 1.f; sn[e] = 0.f; wk[e] = 0.f; }
+  if (hl < 2 * half_lanes) {
+    unpack8(*reinterpret_cast<const uint4*>(a.cos + 2 * (t * a.cs_tok) + 16 * hl), c, bf);
+    unpack8(*reinterpret_cast<const uint4*>(a.sin + 2 * (t * a.cs_tok) + 16 * hl), sn, bf);
+  }
+  unpack8(*reinterpret_cast<const uint4*>(a.qw + 16 * hl), wq, bf);
+  if (HKV) unpack8(*reinterpret_cast<const uint4*>(a.kw + 16 * hl), wk, bf);
+#pragma unroll
+  for (int pr = 0; pr < NP; ++pr) {
+    const int h = 2 * pr + half;
+    float x[8];
+    unpack8(raw[pr], x, bf);
+    qk_row16<T>(x, (h < HQ) ? wq : wk, a.eps, hl, half_lanes, c, sn);
+    if (h < NH) {
+      uint8_t* dst = h < HQ ? a.q_out + 2 * ((t * HQ + h) * 128) : a.k_out + 2 * ((t * HKV + (h - HQ)) * 128);
+      *reinterpret_cast<uint4*>(dst + 16 * hl) = pack8<T>(x);
+    }
   }
   if (a.v_out) {
 #pragma unroll
-    for (int h = 0; h < HKV; ++h)
-      *reinterpret_cast<uint2*>(a.v_out + 2 * ((t * HKV + h) * 128) + 8 * lane) =
-          *reinterpret_cast<const uint2*>(a.v + 2 * (t * a.v_tok + (int64_t)h * a.v_head) + 8 * lane);
+    for (int pr = 0; pr < (HKV + 1) / 2; ++pr) {
+      const int h = 2 * pr + half;
+      if (h < HKV)
+        *reinterpret_cast<uint4*>(a.v_out + 2 * ((t * HKV + h) * 128) + 16 * hl) =
+            *reinterpret_cast<const uint4*>(a.v + 2 * (t * a.v_tok + (int64_t)h * a.v_head) + 16 * hl);
+    }
   }
 }
 
@@ -327,7 +368,11 @@ extern "C" BNA_API int bna_qk_norm_rope(const void* q, int64_t q_tok_stride, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype != BNA_BF16 && dtype != BNA_F16) return fail(BNA_BAD_DTYPE, "qk_norm_rope: bfloat16 or float16 only");
   const bool bf = dtype == BNA_BF16;
-  const bool per_row = tokens <= 64;
+  bool wide_ok = rot % 16 == 0 && q_tok_stride % 8 == 0 && q_head_stride % 8 == 0 && k_tok_stride % 8 == 0 &&
+                 k_head_stride % 8 == 0 && cs_tok_stride % 8 == 0 && (!v || (v_tok_stride % 8 == 0 && v_head_stride % 8 == 0));
+  for (const void* p : {q, k, q_weight, k_weight, cos, sin, v, (const void*)q_out, (const void*)k_out, (const void*)v_out})
+    if (p && (reinterpret_cast<uintptr_t>(p) & 15)) wide_ok = false;
+  const bool per_row = tokens <= 64 || !wide_ok;
   const dim3 grid_rows((unsigned)((tokens * (hq + hkv + (v_out ? hkv : 0)) + kWarps - 1) / kWarps));
 #define BNA_QK_CASE(HQ_, HKV_)                                                                      \
   if (hq == HQ_ && hkv == HKV_) {                                                                    \

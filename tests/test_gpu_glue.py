@@ -67,10 +67,13 @@ def test_qk_norm_rope_matches_eager():
     rq, rk = apply_rotary_pos_emb(rq, rk, cos, sin)
     _close(q.transpose(1, 2), rq)
     _close(k.transpose(1, 2), rk)
-    # decode shapes (one warp per head row instead of per token)
+    # decode shapes (one warp per head row instead of a warp per token; the norm's sum runs
+    # in another order, so within one rounding step)
     q1, k1 = glue.qk_norm_rope(qg[:, -1:, :, :dh], k_raw[:, -1:], qn.weight, kn.weight, cos[:, -1:], sin[:, -1:],
                                qn.eps)
-    assert torch.equal(q1, q[:, -1:]) and torch.equal(k1, k[:, -1:])
+    _close(q1, q[:, -1:], 0.95)
+    _close(k1, k[:, -1:], 0.95)
+    _close(q1.transpose(1, 2), rq[:, :, -1:], 0.95)
 
 
 def test_gate_and_swiglu_match_eager():
