@@ -46,10 +46,12 @@ class CompressedKVCache:
     def _allocate(self, B: int, H: int, dh: int, dtype: torch.dtype, device: torch.device) -> None:
         self.tail_capacity = self.local_window_tokens + 2 * self.max_chunk_size + 2 * self.block_size
         self.summary_capacity = (self.max_kv_size // self.block_size + 4) if self.max_kv_size else 2048
-        self._tail_k = torch.zeros((B, H, self.tail_capacity, dh), dtype=dtype, device=device)
-        self._tail_v = torch.zeros_like(self._tail_k)
-        self._sum_k = torch.zeros((B, H, self.summary_capacity, dh), dtype=dtype, device=device)
-        self._sum_v = torch.zeros_like(self._sum_k)
+        # every kernel reads only ring slots and summary slots it wrote before (the window of
+        # appended positions, closed blocks), so the pools need no clearing
+        self._tail_k = torch.empty((B, H, self.tail_capacity, dh), dtype=dtype, device=device)
+        self._tail_v = torch.empty_like(self._tail_k)
+        self._sum_k = torch.empty((B, H, self.summary_capacity, dh), dtype=dtype, device=device)
+        self._sum_v = torch.empty_like(self._sum_k)
 
     @property
     def ring(self) -> int:
