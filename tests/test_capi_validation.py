@@ -1,0 +1,91 @@
+"""Argument validation of the decoder-glue, decode-GEMV and fused decode-step entry points:
+every rejected call returns its status before touching a device, so these run without a
+GPU.  The Python wrappers refuse CPU tensors (there is no CPU path)."""
+import ctypes
+
+import pytest
+import torch
+
+from butterfly_b200 import _lib, glue
+
+OK, BAD_SHAPE, BAD_STRIDE, BAD_DTYPE, UNSUPPORTED = _lib.OK, _lib.BAD_SHAPE, _lib.BAD_STRIDE, _lib.BAD_DTYPE, _lib.UNSUPPORTED
+P = 1 << 20  # a 16-byte-aligned stand-in pointer: never dereferenced by a rejected call
+BF = _lib.BF16
+
+
+def L():
+    return _lib.lib()
+
+
+def test_rmsnorm_rejections():
+    assert L().bna_rmsnorm(P, 1024, None, 0, P, P, 1024, None, 0, 0, 1024, 1e-6, BF, None) == OK  # no rows: no launch
+    assert L().bna_rmsnorm(P, 1024, None, 0, P, P, 1024, None, 0, 5, 100, 1e-6, BF, None) == UNSUPPORTED
+    assert L().bna_rmsnorm(None, 1024, None, 0, P, P, 1024, None, 0, 5, 1024, 1e-6, BF, None) == BAD_SHAPE
+    assert L().bna_rmsnorm(P + 2, 1024, None, 0, P, P, 1024, None, 0, 5, 1024, 1e-6, BF, None) == BAD_STRIDE
+    assert L().bna_rmsnorm(P, 1020, None, 0, P, P, 1024, None, 0, 5, 1024, 1e-6, BF, None) == BAD_STRIDE
+    assert L().bna_rmsnorm(P, 1024, None, 0, P, P, 1024, P, 1024, 5, 1024, 1e-6, BF, None) == BAD_SHAPE
+    assert L().bna_rmsnorm(P, 1024, None, 0, P, P, 1024, None, 0, 5, 1024, 1e-6, 7, None) == BAD_DTYPE
+    assert b"bfloat16 or float16" in L().bna_last_error()
+
+
+def test_qk_norm_rope_rejections():
+    f = L().bna_qk_norm_rope
+    args = dict(q=P, qt=2560, qh=256, k=P, kt=2560, kh=128, qw=P, kw=P, cos=P, sin=P, cs=32, rot=32, qo=P, ko=P,
+                v=None, vt=0, vh=0, vo=None, tokens=4, hq=8, hkv=2, hd=128, eps=1e-6, dt=BF, s=None)
+
+    def call(**kw):
+        a = dict(args, **kw)
+        return f(*a.values())
+
+    assert call(tokens=0) == OK
+    assert call(hd=64) == UNSUPPORTED
+    assert call(rot=12) == UNSUPPORTED
+    assert call(v=P) == BAD_SHAPE          # v without v_out
+    assert call(q=None) == BAD_SHAPE
+    assert call(qh=255) == BAD_STRIDE
+    assert call(q=P + 2) == BAD_STRIDE
+
+
+def test_gate_and_swiglu_rejections():
+    assert L().bna_gate_sigmoid_mul(P, P, 2560, 256, P, 0, 8, 128, BF, None) == OK
+    assert L().bna_gate_sigmoid_mul(P, P, 2560, 256, P, 4, 8, 12, BF, None) == BAD_SHAPE
+    assert L().bna_gate_sigmoid_mul(P, P, 2561, 256, P, 4, 8, 128, BF, None) == BAD_STRIDE
+    assert L().bna_swiglu(P, 7168, 3584, P, 4, 12, BF, None) == BAD_SHAPE
+    assert L().bna_swiglu(P + 8, 7168, 3584, P, 4, 3584, BF, None) == BAD_STRIDE
+
+
+def test_gemv_rejections():
+    # bna_gemv(x, x_stride, w, out_features, in_features, res, res_stride, out, out_stride, tokens, dtype, stream)
+    assert L().bna_gemv(P, 1024, P, 1024, 1024, None, 0, P, 1024, 9, BF, None) == UNSUPPORTED   # > 8 tokens
+    assert L().bna_gemv(P, 1024, P, 1024, 1000, None, 0, P, 1024, 1, BF, None) == UNSUPPORTED   # K % 256
+    assert L().bna_gemv(P, 16384, P, 1024, 16384, None, 0, P, 1024, 1, BF, None) == UNSUPPORTED  # K > 8192
+    assert L().bna_gemv(P, 1024, P, 0, 1024, None, 0, P, 1024, 1, BF, None) == BAD_SHAPE
+    assert L().bna_gemv(P, 1024, P + 4, 1024, 1024, None, 0, P, 1024, 1, BF, None) == BAD_STRIDE
+    # odd row count with SwiGLU
+    assert L().bna_gemv_rmsnorm(P, 1024, None, 0, P, 1e-6, None, 0, P, 7167, 1024, 1, P, 3583, 1, BF, None) == BAD_SHAPE
+    # sum_out without a residual
+    assert L().bna_gemv_rmsnorm(P, 1024, None, 0, P, 1e-6, P, 1024, P, 2560, 1024, 0, P, 2560, 1, BF, None) == BAD_SHAPE
+    # gated: in_features not a multiple of head_dim
+    assert L().bna_gemv_gated(P, P, 2560, 256, 96, P, 1024, 1024, None, 0, P, 1024, 1, BF, None) == BAD_SHAPE
+
+
+def test_decode_step_qk_rejections():
+    t = _lib.Tensor4()
+    r = _lib.Route()
+    args = [ctypes.byref(t)] * 8 + [None, 0, 0, BF, ctypes.byref(r), 64, 100, 8512, -1, -1, 5, 0.088, P, P, P, P, 32]
+    assert L().bna_decode_step_qk(*args, 12, 1e-6, None) == UNSUPPORTED       # rotary dims not a multiple of 8
+    assert L().bna_decode_step_qk(*args, 32, 1e-6, None) != OK                 # empty tensors: rejected before launch
+    args_bad = list(args)
+    args_bad[20] = None                                                       # null q norm weight
+    assert L().bna_decode_step_qk(*args_bad, 32, 1e-6, None) == BAD_SHAPE
+
+
+def test_python_wrappers_refuse_cpu_tensors():
+    x = torch.zeros(2, 1024, dtype=torch.bfloat16)
+    w = torch.zeros(1024, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        glue.rmsnorm(x, w, 1e-6)
+    with pytest.raises(ValueError):
+        glue.gemv(x, torch.zeros(512, 1024, dtype=torch.bfloat16))
+    with pytest.raises(ValueError):
+        glue.swiglu(torch.zeros(2, 2048, dtype=torch.bfloat16), 1024)
