@@ -233,23 +233,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs a)
       float v = acc[r][m];
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-      acc[r][m] = v;
-      if (S > 1 && lane == 0) part[warp][r][m] = v;
+      if (lane == 0) part[warp][r][m] = v;
     }
-  if (S == 1) {  // one segment: the warp's lanes write its output directly
-    if (!active || lane >= MT || lane >= a.M) return;
-    const int m = lane;
-    float y[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      float t = 0.f;
-#pragma unroll
-      for (int mm = 0; mm < MT; ++mm) t = mm == m ? acc[r][mm] : t;
-      y[r] = t;
-    }
-    gemv_store<T, EPI, R>(a, o, m, y);
-    return;
-  }
   __syncthreads();
   // epilogue: thread = (output of this CTA, token)
   const int tid = threadIdx.x;
