@@ -72,14 +72,9 @@ __device__ __forceinline__ void unpack8f(const uint4& u, float* f, bool bf) {
   }
 }
 
-// Norm weights of this thread's 8-column vectors (v = tid, tid + 256, ...; K <= 8192), loaded
-// before the dependency wait: they are constants, so their latency stays off the critical path.
-constexpr int kMaxNormVec = 4;
-
 // Build x_in [M, K] (storage type) in shared memory.
 template <typename T, int PRO>
-__device__ __forceinline__ void build_input(const GemvArgs& a, uint8_t* xs, float* red,
-                                            const uint4 (&nwv)[kMaxNormVec]) {
+__device__ __forceinline__ void build_input(const GemvArgs& a, uint8_t* xs, float* red) {
   constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
   const int nvec = (int)(a.K >> 3);
   const int tid = threadIdx.x, nth = blockDim.x;
@@ -126,14 +121,11 @@ __device__ __forceinline__ void build_input(const GemvArgs& a, uint8_t* xs, floa
       float tot = 0.f;
       for (int i = 0; i < (nth >> 5); ++i) tot += red[i];
       const float r = rsqrtf(tot / (float)a.K + a.eps);
-#pragma unroll
-      for (int vi = 0; vi < kMaxNormVec; ++vi) {
-        const int v = tid + vi * nth;
-        if (v >= nvec) break;
+      for (int v = tid; v < nvec; v += nth) {
         uint8_t* p = xs + 2 * ((int64_t)m * a.K + v * 8);
         float f[8], w[8];
         unpack8f(*reinterpret_cast<const uint4*>(p), f, bf);
-        unpack8f(nwv[vi], w, bf);
+        unpack8f(ld_nc_128(a.norm_w + 16 * v), w, bf);
 #pragma unroll
         for (int e = 0; e < 8; ++e) f[e] = (f[e] * r) * (1.f + w[e]);
         *reinterpret_cast<uint4*>(p) = make_uint4(ElemTraits<T>::pack2(f[0], f[1]), ElemTraits<T>::pack2(f[2], f[3]),
@@ -143,24 +135,6 @@ __device__ __forceinline__ void build_input(const GemvArgs& a, uint8_t* xs, floa
     }
   }
   __syncthreads();
-}
-
-// Epilogue of output o for token m from its fp32 dot product(s) y (the gate/up pair for SWIGLU).
-template <typename T, int EPI, int R>
-__device__ __forceinline__ void gemv_store(const GemvArgs& a, int o, int m, const float (&y)[R]) {
-  float out;
-  if (EPI == EPI_SWIGLU) {
-    const float g = rnd<T>(y[0]), u = rnd<T>(y[R - 1]);
-    out = rnd<T>(g / (1.f + __expf(-g))) * u;
-  } else {
-    out = rnd<T>(y[0]);
-    if (EPI == EPI_RESID) {
-      const uint16_t rb = *reinterpret_cast<const uint16_t*>(a.res2 + 2 * ((int64_t)m * a.res2_stride + o));
-      out = out + ElemTraits<T>::unpack2((uint32_t)rb).x;
-    }
-  }
-  *reinterpret_cast<uint16_t*>(a.out + 2 * ((int64_t)m * a.out_stride + o)) =
-      (uint16_t)(ElemTraits<T>::pack2(out, 0.f) & 0xFFFFu);
 }
 
 // Warp task = (output, K segment of up to 4 chunks of 256 columns): S segments per output,
@@ -193,17 +167,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs a)
 #pragma unroll
     for (int r = 0; r < R; ++r)
       if (c0 + c < nch) wv[r][c] = ld_nc_128(wrow[r] + 16 * ((c0 + c) * 32 + lane));
-  uint4 nwv[kMaxNormVec];
-  if (PRO == PRO_NORM) {
-#pragma unroll
-    for (int vi = 0; vi < kMaxNormVec; ++vi) {
-      const int v = threadIdx.x + vi * kGemvWarps * 32;
-      if (v < (int)(a.K >> 3)) nwv[vi] = ld_nc_128(a.norm_w + 16 * v);
-    }
-  }
   // the input is produced by the previous kernel of the stream
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  build_input<T, PRO>(a, smem, red, nwv);
+  build_input<T, PRO>(a, smem, red);
   float acc[R][MT];
 #pragma unroll
   for (int r = 0; r < R; ++r)
@@ -250,7 +216,19 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs a)
     for (int sg = 0; sg < S; ++sg) t += part[ole * S + sg][r][m];
     y[r] = t;
   }
-  gemv_store<T, EPI, R>(a, oe, m, y);
+  float out;
+  if (EPI == EPI_SWIGLU) {
+    const float g = rnd<T>(y[0]), u = rnd<T>(y[R - 1]);
+    out = rnd<T>(g / (1.f + __expf(-g))) * u;
+  } else {
+    out = rnd<T>(y[0]);
+    if (EPI == EPI_RESID) {
+      const uint16_t rb = *reinterpret_cast<const uint16_t*>(a.res2 + 2 * ((int64_t)m * a.res2_stride + oe));
+      out = out + ElemTraits<T>::unpack2((uint32_t)rb).x;
+    }
+  }
+  *reinterpret_cast<uint16_t*>(a.out + 2 * ((int64_t)m * a.out_stride + oe)) =
+      (uint16_t)(ElemTraits<T>::pack2(out, 0.f) & 0xFFFFu);
 }
 
 template <typename T, int PRO, int EPI, int MT, int S>

@@ -309,12 +309,6 @@ __global__ void __launch_bounds__(decode_threads(G)) decode_kernel(const ActiveA
     npre = npre < 0 ? 0 : (npre > nraw ? nraw : npre);
     issue_rows(lo, idx_lo, 0, npre, nraw);
   }
-  // q/k norm weights of a fused preparation: constants, loaded before the dependency wait
-  uint2 qn_pre = make_uint2(0, 0), kn_pre = make_uint2(0, 0);
-  if (a.qk_prep) {
-    qn_pre = *reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(a.qn_w) + 8 * lane);
-    kn_pre = *reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(a.kn_w) + 8 * lane);
-  }
   // Launched with programmatic stream serialization: wait for the previous kernel of the
   // stream (and its memory) before touching anything it may write, then let the next
   // kernel start launching.
@@ -373,8 +367,9 @@ __global__ void __launch_bounds__(decode_threads(G)) decode_kernel(const ActiveA
 #pragma unroll 1
     for (int r = warp; r <= G; r += NW) {
       uint8_t* row = r < G ? qraw + r * kDecPitch : kv + (nraw - 1) * kDecPitch;
+      const uint8_t* wp = static_cast<const uint8_t*>(r < G ? a.qn_w : a.kn_w);
       const uint2 u = *reinterpret_cast<const uint2*>(row + 8 * lane);
-      const uint2 uw = r < G ? qn_pre : kn_pre;
+      const uint2 uw = *reinterpret_cast<const uint2*>(wp + 8 * lane);
       float x[4], w[4], c[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
       const float2 x0 = ElemTraits<T>::unpack2(u.x), x1 = ElemTraits<T>::unpack2(u.y);
       const float2 w0 = ElemTraits<T>::unpack2(uw.x), w1 = ElemTraits<T>::unpack2(uw.y);
