@@ -23,7 +23,7 @@ EXPORTED = (
     "bna_prefill_selection_device", "bna_compress_blocks", "bna_compress_kv_blocks", "bna_prefill_attention",
     "bna_active_attention", "bna_cache_append", "bna_decode_step", "bna_prefill_attention_static_scratch",
     "bna_rmsnorm", "bna_qk_norm_rope", "bna_gate_sigmoid_mul", "bna_swiglu", "bna_gemv_rmsnorm", "bna_gemv_gated",
-    "bna_gemv", "bna_launch_probe", "bna_decode_step_qk",
+    "bna_gemv", "bna_launch_probe", "bna_decode_step_qk", "bna_prefill_attention_gated",
 )
 
 
@@ -70,6 +70,8 @@ def lib() -> ctypes.CDLL:
             "bna_compress_blocks": (i32, [T4, T4, i32, i32, i64, i32, i64, i64, i64, vp]),
             "bna_compress_kv_blocks": (i32, [T4, T4, T4, T4, i32, i32, i64, i32, i64, i64, i64, vp]),
             "bna_prefill_attention": (i32, [T4, T4, T4, T4, T4, T4, vp, i64, i64, i32, R, i32, i64, i64, i64, f32, vp]),
+            "bna_prefill_attention_gated": (i32, [T4, T4, T4, T4, T4, T4, T4, vp, i64, i64, i32, R, i32, i64, i64, i64,
+                                                  f32, vp]),
             "bna_active_attention": (i32, [T4, T4, T4, T4, T4, T4, vp, i64, i64, i32, R, i32, vp, i64, i64, i64, i32, f32, vp]),
             "bna_cache_append": (i32, [T4, T4, T4, T4, i32, i64, i64, vp]),
             "bna_prefill_attention_static_scratch": (i32, [T4, T4, T4, T4, vp, i64, i64, i32, R, i32, f32, vp]),

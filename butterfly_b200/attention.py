@@ -137,12 +137,15 @@ def butterfly_compressed_attention(
 
 
 def prefill_with_summaries(q, k, v, layout, window: int, scale: Optional[float] = None, return_lse: bool = False,
-                           k_sum_out: Optional[torch.Tensor] = None, v_sum_out: Optional[torch.Tensor] = None):
+                           k_sum_out: Optional[torch.Tensor] = None, v_sum_out: Optional[torch.Tensor] = None,
+                           gate: Optional[torch.Tensor] = None):
     """Compressor + prefill kernel; returns (out, lse or None, k_sum, v_sum).
 
     The block means land in ``k_sum_out``/``v_sum_out`` [B,Hkv,N,dh] when given (for
     instance a two-pool cache's summary slots, so that a prefill hands its closed blocks
-    to the cache without a copy).  Shapes are checked by the caller."""
+    to the cache without a copy).  With ``gate`` [B,Hq,T,dh] the output is
+    ``out * sigmoid(gate)`` (Qwen3.5's gated attention), applied in the kernel's store;
+    the lse stays that of the ungated attention.  Shapes are checked by the caller."""
     batch, H_q, T, dh = q.shape
     BS, N = int(layout.block_size), int(layout.num_blocks)
     route, _keep = route_for(layout, q.device)
@@ -155,24 +158,44 @@ def prefill_with_summaries(q, k, v, layout, window: int, scale: Optional[float] 
     out = torch.empty((batch, T, H_q, dh), device=q.device, dtype=q.dtype).transpose(1, 2)
     lse = torch.empty((batch, H_q, T), device=q.device, dtype=torch.float32) if return_lse else None
     sc = float(scale) if scale is not None else 1.0 / math.sqrt(dh)
-    prefill_attention_into(q, k, v, ks, vs, out, lse, route, int(window), sc)
+    if gate is not None and not prefill_attention_into(q, k, v, ks, vs, out, lse, route, int(window), sc, gate=gate):
+        from . import glue  # window beyond the fused kernel's ring: gate in a separate launch
+        out = glue.gate_sigmoid_mul(out.transpose(1, 2), gate.transpose(1, 2)).view(
+            batch, T, H_q, dh).transpose(1, 2)
+    elif gate is None:
+        prefill_attention_into(q, k, v, ks, vs, out, lse, route, int(window), sc)
     return out, lse, ks, vs
 
 
 def prefill_attention_into(q, k, v, k_sum, v_sum, out, lse, route, window: int, scale: float, *,
-                           q_pos0: int = 0, kv_pos0: int = 0, total_len: Optional[int] = None) -> None:
+                           q_pos0: int = 0, kv_pos0: int = 0, total_len: Optional[int] = None,
+                           gate: Optional[torch.Tensor] = None) -> bool:
     """Launch the tcgen05 prefill kernel on pre-computed summaries (no allocation).
 
     Query row i is at global position q_pos0 + i and key row j at kv_pos0 + j; the
-    routing covers a sequence of ``total_len`` tokens (default: q_pos0 + Tq)."""
+    routing covers a sequence of ``total_len`` tokens (default: q_pos0 + Tq).  With
+    ``gate`` [B,Hq,Tq,dh] the store writes ``out * sigmoid(gate)``; when the window is
+    too large for the gated kernel the ungated output is written and False is returned
+    (the caller gates it), else True."""
     T = int(q.shape[2])
     tot = q_pos0 + T if total_len is None else int(total_len)
     lp, lb, lh = _lse_args(lse)
     tq, tk, tv, tks, tvs, to = (_lib.t4(x) for x in (q, k, v, k_sum, v_sum, out))
-    _lib.check(_lib.lib().bna_prefill_attention(
-        ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv), ctypes.byref(tks), ctypes.byref(tvs),
-        ctypes.byref(to), lp, lb, lh, _lib.dtype_code(q.dtype), ctypes.byref(route), int(window), int(q_pos0),
-        int(kv_pos0), tot, float(scale), _lib.stream_ptr(q.device)))
+    L = _lib.lib()
+    args_tail = (ctypes.byref(to), lp, lb, lh, _lib.dtype_code(q.dtype), ctypes.byref(route), int(window),
+                 int(q_pos0), int(kv_pos0), tot, float(scale), _lib.stream_ptr(q.device))
+    if gate is not None:
+        if gate.dtype != q.dtype or tuple(gate.shape) != tuple(out.shape):
+            raise ValueError("gate must match the output's shape and dtype")
+        tg = _lib.t4(gate)
+        st = L.bna_prefill_attention_gated(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv), ctypes.byref(tks),
+                                           ctypes.byref(tvs), ctypes.byref(tg), *args_tail)
+        if st != _lib.UNSUPPORTED:
+            _lib.check(st)
+            return True
+    _lib.check(L.bna_prefill_attention(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv), ctypes.byref(tks),
+                                       ctypes.byref(tvs), *args_tail))
+    return gate is None
 
 
 def butterfly_compressed_attention_active(

@@ -25,7 +25,7 @@ int check_cuda(cudaError_t e, const char* what) {
 
 int launch_prefill(const bna_tensor4*, const bna_tensor4*, const bna_tensor4*, const bna_tensor4*,
                    const bna_tensor4*, bna_tensor4*, float*, int64_t, int64_t, int, const bna_route*, int,
-                   int64_t, int64_t, int64_t, float, cudaStream_t);
+                   int64_t, int64_t, int64_t, float, cudaStream_t, const bna_tensor4* = nullptr);
 int launch_compress(const bna_tensor4*, bna_tensor4*, int, int, int64_t, int, int64_t, int64_t, int64_t,
                     cudaStream_t, const bna_tensor4*, bna_tensor4*);
 int launch_append(bna_tensor4*, bna_tensor4*, const bna_tensor4*, const bna_tensor4*, int64_t, int64_t,
@@ -229,11 +229,11 @@ int bna_compress_kv_blocks(const bna_tensor4* k, const bna_tensor4* v, bna_tenso
                          v, v_out);
 }
 
-int bna_prefill_attention(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4* v,
-                          const bna_tensor4* k_sum, const bna_tensor4* v_sum, bna_tensor4* out, float* lse,
-                          int64_t lse_stride_b, int64_t lse_stride_h, int32_t dtype, const bna_route* route,
-                          int32_t window, int64_t q_pos0, int64_t kv_pos0, int64_t total_len, float scale,
-                          void* stream) {
+static int prefill_impl(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4* v,
+                        const bna_tensor4* k_sum, const bna_tensor4* v_sum, bna_tensor4* out, float* lse,
+                        int64_t lse_stride_b, int64_t lse_stride_h, int32_t dtype, const bna_route* route,
+                        int32_t window, int64_t q_pos0, int64_t kv_pos0, int64_t total_len, float scale,
+                        void* stream, const bna_tensor4* gate) {
   if (int rc = check_dtype(dtype)) return rc;
   if (int rc = check_route(route)) return rc;
   if (null4(q) || null4(k) || null4(v) || null4(k_sum) || null4(v_sum) || null4(out))
@@ -263,8 +263,33 @@ int bna_prefill_attention(const bna_tensor4* q, const bna_tensor4* k, const bna_
     return fail(BNA_BAD_SHAPE, "summary tensors must be [B, Hkv, >= num_blocks, dh]");
   if (B * Hkv * ((Tq * G + 127) / 128) > (int64_t)1 << 31) return fail(BNA_UNSUPPORTED, "problem too large");
   if (!(scale > 0.f) || !std::isfinite(scale)) return fail(BNA_BAD_SHAPE, "scale must be positive");
+  if (gate) {
+    if (null4(gate)) return fail(BNA_BAD_SHAPE, "null gate tensor");
+    if (int rc = check_rows(gate, "gate", dh)) return rc;
+    if (gate->size[0] != B || gate->size[1] != Hq || gate->size[2] != Tq)
+      return fail(BNA_BAD_SHAPE, "gate shape must equal out shape");
+  }
   return launch_prefill(q, k, v, k_sum, v_sum, out, lse, lse_stride_b, lse_stride_h, dtype, route, window, q_pos0,
-                        kv_pos0, total_len, scale, (cudaStream_t)stream);
+                        kv_pos0, total_len, scale, (cudaStream_t)stream, gate);
+}
+
+int bna_prefill_attention(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4* v,
+                          const bna_tensor4* k_sum, const bna_tensor4* v_sum, bna_tensor4* out, float* lse,
+                          int64_t lse_stride_b, int64_t lse_stride_h, int32_t dtype, const bna_route* route,
+                          int32_t window, int64_t q_pos0, int64_t kv_pos0, int64_t total_len, float scale,
+                          void* stream) {
+  return prefill_impl(q, k, v, k_sum, v_sum, out, lse, lse_stride_b, lse_stride_h, dtype, route, window, q_pos0,
+                      kv_pos0, total_len, scale, stream, nullptr);
+}
+
+int bna_prefill_attention_gated(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4* v,
+                                const bna_tensor4* k_sum, const bna_tensor4* v_sum, const bna_tensor4* gate,
+                                bna_tensor4* out, float* lse, int64_t lse_stride_b, int64_t lse_stride_h,
+                                int32_t dtype, const bna_route* route, int32_t window, int64_t q_pos0,
+                                int64_t kv_pos0, int64_t total_len, float scale, void* stream) {
+  if (!gate) return fail(BNA_BAD_SHAPE, "null gate tensor");
+  return prefill_impl(q, k, v, k_sum, v_sum, out, lse, lse_stride_b, lse_stride_h, dtype, route, window, q_pos0,
+                      kv_pos0, total_len, scale, stream, gate);
 }
 
 static int check_active_common(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4* v,

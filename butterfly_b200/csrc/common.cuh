@@ -45,6 +45,12 @@ template <> struct ElemTraits<__nv_bfloat16> {
     __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&u);
     return __bfloat1622float2(h);
   }
+  // element-wise product of two packed pairs, rounded once: the fp32 product of two 16-bit
+  // values is exact, so this equals rounding the fp32 product
+  __device__ static __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+    __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+  }
 };
 template <> struct ElemTraits<__half> {
   static constexpr uint32_t kUmmaFormat = 0;
@@ -56,6 +62,10 @@ template <> struct ElemTraits<__half> {
   __device__ static __forceinline__ float2 unpack2(uint32_t u) {
     __half2 h = *reinterpret_cast<__half2*>(&u);
     return __half22float2(h);
+  }
+  __device__ static __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+    __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
   }
 };
 
@@ -106,6 +116,15 @@ __device__ __forceinline__ uint4 ld_nc_128(const void* p) {
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                : "l"(p));
   return r;
+}
+// 1 / (1 + e^-x) from the fast exponential and the fast divide (two MUFU operations, no
+// IEEE division sequence); callers round the result to 16 bits, where its few-ulp fp32
+// error is invisible except at rounding ties.  Saturates to 0 below x ~ -87.
+__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+
+// Pull the 128-byte line holding p into L2 (no registers held while it is in flight).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 __device__ __forceinline__ uint4 ld_128(const void* p) {
   uint4 r;

@@ -90,7 +90,7 @@ __device__ __forceinline__ void build_input(const GemvArgs& a, uint8_t* xs, floa
         unpack8f(ld_128(a.x + 2 * ((int64_t)m * a.K + c)), f, bf);
         unpack8f(ld_128(a.gate + 2 * ((int64_t)m * a.g_tok + (int64_t)h * a.g_head + d)), g, bf);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = f[e] * rnd<T>(1.f / (1.f + __expf(-g[e])));
+        for (int e = 0; e < 8; ++e) f[e] = f[e] * rnd<T>(sigmoid_fast(g[e]));
       } else {
         unpack8f(ld_128(a.x + 2 * ((int64_t)m * a.x_stride + v * 8)), f, bf);
         if (PRO == PRO_NORM && a.res) {

@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(256) gate_mul_kernel(const GateArgs a) {
   unpack8(ld_nc_128(a.g + 2 * ((int64_t)t * a.g_tok + (int64_t)h * a.g_head + c * 8)), g, bf);
   float y[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) y[e] = o[e] * round_to<T>(1.f / (1.f + __expf(-g[e])));
+  for (int e = 0; e < 8; ++e) y[e] = o[e] * round_to<T>(sigmoid_fast(g[e]));
   st_128(a.out + 16 * (int64_t)i, pack8<T>(y));
 }
 

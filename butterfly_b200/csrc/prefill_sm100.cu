@@ -60,6 +60,10 @@ struct PrefillArgs {
   int o_st256;  // output base and strides are 32-byte multiples: 256-bit stores
   float* lse;
   int64_t ls_b, ls_h;
+  // optional output gate (the attention output gate of a gated q_proj): when non-null the
+  // kernel writes round(O) * round(sigmoid(gate)) instead of O; element strides like out
+  const void* gate;
+  int64_t gs_b, gs_h, gs_t;
   int* err;         // device error word
   uint64_t* trace;  // optional timeline: [cta][unit < 64][16] globaltimer stamps
 };
@@ -100,7 +104,7 @@ __device__ __noinline__ int prefill_summaries_ool(const bna_route& r, int blk, i
   return prefill_summaries(r, blk, window, r.neighbors, ids);
 }
 
-template <typename T, int NR_>
+template <typename T, int NR_, bool GATED>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ PrefillArgs a) {
@@ -377,6 +381,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool e_valid = false;
     float e_mb = 0.f;
     auto epilogue = [&](int i) -> bool {
+      // gate values of this row's 32 output columns (pulled into L2 a unit earlier), read
+      // into registers per 16 columns at the store
+      const bool gated = GATED && e_valid;
+      const uint8_t* gp = nullptr;
+      if (gated)
+        gp = reinterpret_cast<const uint8_t*>(a.gate) +
+             2 * (e_b * a.gs_b + (int64_t)(e_kvh * G + g) * a.gs_h + (int64_t)e_qloc * a.gs_t) + cq * 64;
       if (!mbar_wait(&pvdone[i & 3], (uint32_t)(i >> 2) & 1u, abort_flag, 5, a.err)) return false;
       if (row == 0 && cq == 0) stamp(i, 7);
       tc_fence_after();
@@ -394,8 +405,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c0 = 0; c0 < 32; c0 += 16) {
           uint32_t w[8];
+          uint4 gv[2] = {};
+          if (gated) {
+            gv[0] = ld_nc_128(gp + c0 * 2);
+            gv[1] = ld_nc_128(gp + c0 * 2 + 16);
+          }
 #pragma unroll
-          for (int j = 0; j < 8; ++j) w[j] = ElemTraits<T>::pack2_fast(o[c0 + 2 * j] * inv, o[c0 + 2 * j + 1] * inv);
+          for (int j = 0; j < 8; ++j) {
+            w[j] = ElemTraits<T>::pack2_fast(o[c0 + 2 * j] * inv, o[c0 + 2 * j + 1] * inv);
+            if (gated) {  // as the eager ops: round(round(O) * round(sigmoid(gate)))
+              const uint32_t gw = j % 4 == 0 ? gv[j / 4].x : j % 4 == 1 ? gv[j / 4].y : j % 4 == 2 ? gv[j / 4].z : gv[j / 4].w;
+              const float2 gg = ElemTraits<T>::unpack2(gw);
+              w[j] = ElemTraits<T>::mul2(w[j], ElemTraits<T>::pack2(sigmoid_fast(gg.x), sigmoid_fast(gg.y)));
+            }
+          }
           if (a.o_st256) {
             st_256(orow + c0 * 2, w);
           } else {
@@ -417,6 +440,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int qs = t * QT;
       const int qloc = qs + qi;
       const bool valid_row = qloc < a.Tq;
+      if (GATED && valid_row)  // the gate row this unit's epilogue reads, one unit from now
+        prefetch_l2(reinterpret_cast<const uint8_t*>(a.gate) +
+                    2 * (b * a.gs_b + (int64_t)(kvh * G + g) * a.gs_h + (int64_t)qloc * a.gs_t) + cq * 64);
       // positions fit in 32 bits (checked on the host); no 64-bit division on this path
       const int qglob = a.q_pos0_i + qloc;
       const int kstart = a.q_pos0_i + qs - (a.window - 1);
@@ -603,8 +629,12 @@ static int encode_map(CUtensorMap* m, const bna_tensor4* t, CUtensorMapDataType 
 int launch_prefill(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4* v, const bna_tensor4* ks,
                    const bna_tensor4* vs, bna_tensor4* out, float* lse, int64_t ls_b, int64_t ls_h, int dtype,
                    const bna_route* route, int window, int64_t q_pos0, int64_t kv_pos0, int64_t total_len,
-                   float scale, cudaStream_t stream) {
+                   float scale, cudaStream_t stream, const bna_tensor4* gate) {
   PrefillArgs a{};
+  if (gate) {
+    a.gate = gate->data;
+    a.gs_b = gate->stride[0]; a.gs_h = gate->stride[1]; a.gs_t = gate->stride[2];
+  }
   a.B = (int)q->size[0];
   a.Hq = (int)q->size[1];
   a.Tq = (int)q->size[2];
@@ -653,9 +683,11 @@ int launch_prefill(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4
   a.QS = 3;
   if ((int)PrefillSmem(a.NR, a.QT, 3).total > max_smem) a.QS = 2;
   const uint32_t smem = PrefillSmem(a.NR, a.QT, a.QS).total;
-  if ((int)smem > max_smem)  // rings too large for this shape: stage-based variant
+  if ((int)smem > max_smem) {  // rings too large for this shape: stage-based variant
+    if (gate) return fail(BNA_UNSUPPORTED, "the gated epilogue needs the ring-based kernel (window too large)");
     return staged::launch_prefill_staged(q, k, v, ks, vs, out, lse, ls_b, ls_h, dtype, route, window, q_pos0, kv_pos0,
                                          total_len, scale, stream);
+  }
 
   const CUtensorMapDataType dt = dtype == BNA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap mq, mk, mv;
@@ -695,8 +727,13 @@ int launch_prefill(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4
   };
 #define BNA_PREFILL_CASE(NRV)                                          \
   case NRV:                                                            \
-    if (dtype == BNA_BF16) launch(prefill_sm100_kernel<__nv_bfloat16, NRV>); \
-    else launch(prefill_sm100_kernel<__half, NRV>);                    \
+    if (gate) {                                                        \
+      if (dtype == BNA_BF16) launch(prefill_sm100_kernel<__nv_bfloat16, NRV, true>); \
+      else launch(prefill_sm100_kernel<__half, NRV, true>);            \
+    } else {                                                           \
+      if (dtype == BNA_BF16) launch(prefill_sm100_kernel<__nv_bfloat16, NRV, false>); \
+      else launch(prefill_sm100_kernel<__half, NRV, false>);           \
+    }                                                                  \
     break;
   switch (a.NR) {
     BNA_PREFILL_CASE(16) BNA_PREFILL_CASE(32) BNA_PREFILL_CASE(48) BNA_PREFILL_CASE(64)

@@ -9,8 +9,9 @@ rotary-embedding concatenations, separate sigmoid / SiLU / multiply / residual p
     h   = rmsnorm(x)                                  one kernel   (input_layernorm)
     qkv = h @ [Wq; Wk; Wv]^T                          one GEMM     (q/k/v projections merged)
     q,k = qk_norm_rope(q part, k part)                one kernel   (q_norm/k_norm + partial RoPE)
-    o   = compressed attention (prefill / decode)     the path's kernels
-    y   = o * sigmoid(gate)                           one kernel
+    y   = attention(q,k,v) * sigmoid(gate)            the path's kernels (whole-prompt prefill: the
+                                                      gate is applied in the attention kernel's store;
+                                                      otherwise one more kernel)
     a   = y @ Wo^T                                    one GEMM
     x2, h2 = x + a, rmsnorm(x + a)                    one kernel   (residual + post_attention_layernorm)
     gu  = h2 @ [Wg; Wu]^T                             one GEMM     (gate/up merged)
@@ -103,6 +104,7 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
     k_raw = qkv[..., nq:nq + hkv * dh].view(B, T, hkv, dh)
     v = qkv[..., nq + hkv * dh:].view(B, T, hkv, dh)
     cos, sin = position_embeddings
+    gated = None  # the gated attention output [B,T,hq*dh] when the gate rode along with attention
     if attn._shard is not None:
         # sequence shard: K and V go straight into buffers whose first W-1 rows receive the
         # previous rank's halo
@@ -123,7 +125,13 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
         qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
         if comp_cache is None and past_key_values is not None:
             kt, vt = past_key_values.update(kt, vt, attn.layer_idx)
-        out, backend, hit = attn.attend(qt, kt, vt, comp_cache, cache_len, k_len_after, kwargs.get("cache_position"))
+        if decode:  # the gate rides along with the o_proj GEMV
+            out, backend, hit = attn.attend(qt, kt, vt, comp_cache, cache_len, k_len_after,
+                                            kwargs.get("cache_position"))
+        else:
+            out, backend, hit = attn.attend(qt, kt, vt, comp_cache, cache_len, k_len_after,
+                                            kwargs.get("cache_position"), gate=qg[..., dh:].transpose(1, 2))
+            gated = out.transpose(1, 2).reshape(B, T, hq * dh)
     if decode:
         x2 = glue.gemv_gated(out.transpose(1, 2).reshape(B, hq, dh), qg[:, 0, :, dh:], src.o_proj.weight,
                              residual=x.view(B, H))
@@ -132,7 +140,10 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
         x3 = glue.gemv(act, self.mlp.down_proj.weight, residual=x2)
         attn._profile(T, k_len_after, backend, hit, t0, fused=True)
         return x3.view(B, 1, H)
-    y = glue.gate_sigmoid_mul(out.transpose(1, 2), qg[..., dh:])  # out storage is [B,T,hq,dh]
+    if gated is None:
+        y = glue.gate_sigmoid_mul(out.transpose(1, 2), qg[..., dh:])  # out storage is [B,T,hq,dh]
+    else:
+        y = gated
     a = F.linear(y, src.o_proj.weight)
     h2, x2 = glue.rmsnorm(a, self.post_attention_layernorm.weight, self.post_attention_layernorm.eps,
                           residual=x, want_sum=True)

@@ -35,6 +35,7 @@ import torch
 import torch.nn as nn
 
 from .. import attention as _attn
+from .. import glue
 from ..cache import CompressedKVCache
 from ..topology import build_block_butterfly_layout
 
@@ -428,12 +429,16 @@ class QwenCUDAButterflyAttention(nn.Module):
             raise ValueError(f"compressed Butterfly kernels need head_dim 128, layer has {self.head_dim}")
         return reason, comp_cache, cache_len, k_len_after
 
-    def attend(self, q, k, v, comp_cache, cache_len: int, k_len_after: int, cache_position=None, qk_prep=None):
+    def attend(self, q, k, v, comp_cache, cache_len: int, k_len_after: int, cache_position=None, qk_prep=None,
+               gate=None):
         """Compressed attention of q [B,Hq,Tq,dh] over k/v [B,Hkv,Tk,dh] (HF-cache history
         included, or the new tokens only when ``comp_cache`` holds the history).  Returns
         ([B,Hq,Tq,dh] view of [B,Tq,Hq,dh] storage, backend name, layout-cache hit).
         ``qk_prep`` (a decode step into ``comp_cache`` only): q / k are raw projection rows and
-        the step applies the q/k norm and rotary embedding itself (see decode_step)."""
+        the step applies the q/k norm and rotary embedding itself (see decode_step).
+        ``gate`` [B,Hq,Tq,dh]: return ``out * sigmoid(gate)`` (Qwen3.5's output gate), fused
+        into the prefill kernel's store on whole-prompt prefills, a separate launch otherwise."""
+        gated = False
         q_len = int(q.shape[2])
         W = int(self.cfg.compressed_local_window_tokens)
         scale = 1.0 / math.sqrt(self.head_dim)  # SDPA's default, as the reference (the module scaling is not passed)
@@ -449,7 +454,8 @@ class QwenCUDAButterflyAttention(nn.Module):
                 comp_cache.reserve(k.shape[0], k.shape[1], k.shape[3], k.dtype, k.device)
                 slots = comp_cache.summary_slots(lay.num_blocks)
                 ks_out, vs_out = slots if slots is not None else (None, None)
-                out, _, ks, vs = _attn.prefill_with_summaries(q, k, v, lay, W, scale, False, ks_out, vs_out)
+                out, _, ks, vs = _attn.prefill_with_summaries(q, k, v, lay, W, scale, False, ks_out, vs_out, gate=gate)
+                gated = True
                 comp_cache.adopt_prefill(k, v, ks, vs)
                 backend = "compressed_prefill+cache_handoff"
             else:
@@ -462,9 +468,17 @@ class QwenCUDAButterflyAttention(nn.Module):
             out = _attn.butterfly_compressed_attention_active(q, k, v, layout=lay, query_positions=pos,
                                                              local_window_tokens=W, scale=scale)
             backend = "compressed_butterfly_active"
+        elif gate is not None:
+            out = _attn.prefill_with_summaries(q, k, v, lay, W, scale, gate=gate)[0]
+            gated = True
+            backend = "compressed_butterfly"
         else:
             out = _attn.butterfly_compressed_attention(q, k, v, layout=lay, local_window_tokens=W, scale=scale)
             backend = "compressed_butterfly"
+        if gate is not None and not gated:
+            B, Hq, Tq, dh = out.shape
+            out = glue.gate_sigmoid_mul(out.transpose(1, 2).contiguous(), gate.transpose(1, 2)).view(
+                B, Tq, Hq, dh).transpose(1, 2)
         return out, backend, hit
 
     def attend_sharded(self, q, k_ext, v_ext, halo: int):

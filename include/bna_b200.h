@@ -154,6 +154,20 @@ BNA_API int bna_prefill_attention(const bna_tensor4* q, const bna_tensor4* k, co
                           const bna_route* route, int32_t window, int64_t q_pos0, int64_t kv_pos0,
                           int64_t total_len, float scale, void* stream);
 
+/* The same with the output gate of Qwen3.5's gated attention fused into the store:
+ * out = round(round(o) * round(sigmoid(gate))) for gate [B,Hq,Tq,dh] (the q-projection's
+ * gate half, same dtype and row rules as q), the rounding of the separate
+ * bna_gate_sigmoid_mul after an ungated call (Qwen3_5Attention.forward,
+ * transformers/models/qwen3_5/modeling_qwen3_5.py, `attn_output * torch.sigmoid(gate)`).
+ * Windows too large for the ring-based kernel return BNA_UNSUPPORTED (call the ungated
+ * entry point and gate separately). */
+BNA_API int bna_prefill_attention_gated(const bna_tensor4* q, const bna_tensor4* k, const bna_tensor4* v,
+                                        const bna_tensor4* k_sum, const bna_tensor4* v_sum,
+                                        const bna_tensor4* gate, bna_tensor4* out, float* lse,
+                                        int64_t lse_stride_b, int64_t lse_stride_h, int32_t dtype,
+                                        const bna_route* route, int32_t window, int64_t q_pos0,
+                                        int64_t kv_pos0, int64_t total_len, float scale, void* stream);
+
 /* ---- K4: active / decode attention (:1125-1197; MLX from_cache :1669-1876) -------------
  * One query row per (b, query index).  Raw keys for position p are the positions
  * [max(0,p-W+1), p]; position x is read at k[b,h,x % ring] (ring > 0) or

@@ -229,3 +229,28 @@ def test_decode_step_with_fused_qk_prep_equals_separate_kernels():
     for x, y in zip(caches[0].state, caches[1].state):
         assert torch.equal(x, y)
 
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("G,W", [(4, 64), (1, 64), (8, 32), (2, 130)])
+def test_prefill_gated_epilogue_equals_separate_gate(dtype, G, W):
+    """bna_prefill_attention_gated (the output gate applied in the prefill kernel's store)
+    writes exactly what bna_prefill_attention followed by bna_gate_sigmoid_mul writes; a
+    window beyond the ring-based kernel gates in a separate launch with the same result."""
+    import butterfly_b200 as bb
+    from butterfly_b200 import attention as A
+    g = torch.Generator(device="cuda").manual_seed(9 + G)
+    B, Hkv, T, dh = 2, 2, 1000, 128
+    Hq = Hkv * G
+    qg = (torch.randn(B, T, Hq, 2 * dh, device="cuda", generator=g) * 3).to(dtype)
+    q = qg[..., :dh].transpose(1, 2)
+    gate = qg[..., dh:].transpose(1, 2)
+    k = torch.randn(B, T, Hkv, dh, device="cuda", generator=g).to(dtype).transpose(1, 2)
+    v = torch.randn(B, T, Hkv, dh, device="cuda", generator=g).to(dtype).transpose(1, 2)
+    lay = bb.build_block_butterfly_layout(seq_len=T, block_size=128, num_key_value_heads=Hkv, num_key_value_groups=G,
+                                          layer_idx=3, local_window_blocks=1, sink_count=1, partner_count=1,
+                                          partner_rule="causal_shift")
+    out, _, _, _ = A.prefill_with_summaries(q, k, v, lay, W, None)
+    ref = glue.gate_sigmoid_mul(out.transpose(1, 2), gate.transpose(1, 2))
+    got, _, _, _ = A.prefill_with_summaries(q, k, v, lay, W, None, gate=gate)
+    assert torch.equal(got.transpose(1, 2).reshape(B, T, Hq * dh), ref)
