@@ -147,6 +147,24 @@ def swiglu(gate_up: torch.Tensor, inter: int) -> torch.Tensor:
     return out
 
 
+def gemm_swiglu(h: torch.Tensor, w_gate_up: torch.Tensor, inter: int) -> torch.Tensor:
+    """silu(h @ Wg^T) * (h @ Wu^T) for h [..., K] and w_gate_up [2*inter, K] = [Wg; Wu], on
+    the tcgen05 GEMM with SwiGLU in its epilogue -> [..., inter] (the [.., 2*inter]
+    product never reaches HBM)."""
+    _lib.require_cuda(h, w_gate_up)
+    K = int(h.shape[-1])
+    rows, ldh = _rows(h, K)
+    if w_gate_up.dim() != 2 or int(w_gate_up.shape[0]) != 2 * inter or int(w_gate_up.shape[1]) != K:
+        raise ValueError(f"w_gate_up must be [2*inter, K] = [{2 * inter}, {K}], got {tuple(w_gate_up.shape)}")
+    if w_gate_up.stride(1) != 1 or w_gate_up.dtype != h.dtype:
+        raise ValueError("w_gate_up must be row-major with h's dtype")
+    out = torch.empty((*h.shape[:-1], inter), device=h.device, dtype=h.dtype)
+    _lib.check(_lib.lib().bna_gemm_swiglu(h.data_ptr(), ldh, w_gate_up.data_ptr(), w_gate_up.stride(0),
+                                          out.data_ptr(), inter, rows, K, inter, _lib.dtype_code(h.dtype),
+                                          _lib.stream_ptr(h.device)))
+    return out
+
+
 def _mat(x: torch.Tensor, K: int) -> tuple[int, int]:
     """(tokens, row stride) of a [M, K] matrix view with a contiguous last dim."""
     if x.dim() != 2 or x.shape[1] != K or x.stride(1) != 1:

@@ -14,8 +14,8 @@ rotary-embedding concatenations, separate sigmoid / SiLU / multiply / residual p
                                                       otherwise one more kernel)
     a   = y @ Wo^T                                    one GEMM
     x2, h2 = x + a, rmsnorm(x + a)                    one kernel   (residual + post_attention_layernorm)
-    gu  = h2 @ [Wg; Wu]^T                             one GEMM     (gate/up merged)
-    x2 += swiglu(gu) @ Wd^T                           one kernel + one GEMM accumulating into x2
+    act = silu(h2 @ Wg^T) * (h2 @ Wu^T)               one tcgen05 GEMM, SwiGLU in its epilogue
+    x2 += act @ Wd^T                                  one GEMM accumulating into x2
 
 For a decode step (one token per sequence, up to 8 sequences) the projections are instead
 weight-streaming GEMV kernels with the neighbouring steps fused in: rmsnorm+qkv,
@@ -75,6 +75,8 @@ class _FusedState:
         self.w_gu = _merge_weights([mlp.gate_proj, mlp.up_proj])
         self.hq, self.hkv, self.dh = attn.num_heads, attn.num_key_value_heads, attn.head_dim
         self.inter = mlp.gate_proj.out_features
+        # the tcgen05 gate/up GEMM tiles K by 64 and the intermediate size by 128
+        self.gemm_swiglu = mlp.gate_proj.in_features % 64 == 0 and self.inter % 128 == 0
 
 
 def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=None, attention_mask=None,
@@ -147,8 +149,10 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
     a = F.linear(y, src.o_proj.weight)
     h2, x2 = glue.rmsnorm(a, self.post_attention_layernorm.weight, self.post_attention_layernorm.eps,
                           residual=x, want_sum=True)
-    gu = F.linear(h2, st.w_gu)
-    act = glue.swiglu(gu, st.inter)
+    if st.gemm_swiglu:  # gate/up GEMM with SwiGLU in the epilogue (no [T, 2*inter] product in HBM)
+        act = glue.gemm_swiglu(h2, st.w_gu, st.inter)
+    else:
+        act = glue.swiglu(F.linear(h2, st.w_gu), st.inter)
     x2.view(-1, H).addmm_(act.view(-1, st.inter), self.mlp.down_proj.weight.t())
     attn._profile(T, k_len_after, backend, hit, t0, fused=True)
     return x2

@@ -244,6 +244,16 @@ BNA_API int bna_gate_sigmoid_mul(const void* o, const void* gate, int64_t gate_t
 BNA_API int bna_swiglu(const void* gate_up, int64_t row_stride, int64_t up_offset, void* out, int64_t rows,
                        int32_t inter, int32_t dtype, void* stream);
 
+/* The gate/up projection with SwiGLU in the epilogue, on tcgen05 tensor cores:
+ * out[m, i] = silu(h[m,:] . w[i,:]) * (h[m,:] . w[inter + i,:]) for m < M, i < inter, with h
+ * [M, K] (row stride ldh), w [2*inter, K] (gate rows, then up rows; row stride ldw) and out
+ * [M, inter] (row stride ldo), all row-major.  The gate and up products, silu(gate) and the
+ * product are each rounded to the 16-bit type, as the eager ops (transformers'
+ * Qwen3_5MLP: act_fn(gate_proj(x)) * up_proj(x)); accumulation is fp32.  K a multiple of 64,
+ * inter of 128, row strides multiples of 8 elements, pointers 16-byte aligned. */
+BNA_API int bna_gemm_swiglu(const void* h, int64_t ldh, const void* w, int64_t ldw, void* out, int64_t ldo,
+                            int64_t M, int32_t K, int32_t inter, int32_t dtype, void* stream);
+
 /* Decode-time projections for 1..8 tokens (y = W x per token, W [out_features,
  * in_features] row-major, in_features a multiple of 256), with the layer step before the
  * projection fused in front of it and the one after it fused behind it.  Replace the
