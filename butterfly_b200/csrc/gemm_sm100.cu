@@ -1,26 +1,38 @@
-// gemm_sm100.cu — the Qwen3.5 MLP's gate/up projection with SwiGLU in the epilogue, on
-// Blackwell tensor cores.
+// gemm_sm100.cu — projections of the Qwen3.5 decoder layer on Blackwell tensor cores, with
+// the elementwise step that follows each one applied in the epilogue.
 //
-//   act[m, j] = silu(h[m,:] . Wg[j,:]) * (h[m,:] . Wu[j,:])       Wg = W[0:I], Wu = W[I:2I]
+// Two epilogues share one persistent tcgen05 GEMM (out = h . W^T, fp32 accumulation):
 //
-// It replaces the merged gate/up GEMM followed by the SwiGLU kernel of the fused decoder
-// layer (transformers' Qwen3_5MLP: down_proj(act_fn(gate_proj(x)) * up_proj(x))): the
-// [M, 2I] gate/up product never reaches HBM.  Rounding follows the eager ops: the gate and
-// up products are rounded to the 16-bit type, silu(gate) is rounded, and so is the product.
+//  * SwiGLU (the MLP's gate/up projection, transformers' Qwen3_5MLP
+//    down_proj(act_fn(gate_proj(x)) * up_proj(x))):
+//        act[m, j] = silu(h[m,:] . Wg[j,:]) * (h[m,:] . Wu[j,:])     Wg = W[0:I], Wu = W[I:2I]
+//    A tile pairs 128 gate rows with the 128 matching up rows of W, so one M = 128, N = 256
+//    accumulator holds both halves of 128 output columns; the [M, 2I] gate/up product never
+//    reaches HBM.  The gate and up products, silu(gate) and the product are each rounded to
+//    the 16-bit type, as the eager ops.
 //
-// Tiles: 128 rows of h x (128 gate rows + the 128 matching up rows of W), so one
-// M = 128, N = 256 accumulator holds both halves of 128 output columns.  K advances in
-// 64-element (128-byte) blocks: per block TMA loads a 16 KB h tile and two 16 KB W tiles
-// (gate rows j0.., up rows I + j0..) into one 4-stage ring; placed back to back, the two W
-// tiles form the 256-row K-major B operand.  Persistent CTAs (one per SM) walk the tiles
-// with the output column tile innermost, so the CTAs in flight share h rows through L2.
+//  * q/k norm + RoPE (the attention's merged q/k/v projection; Qwen3_5Attention.forward and
+//    bna/integrations/qwen_torch.py:535-573: q_norm / k_norm per head, then the rotary
+//    embedding in rotate-half form on the first `rot` dims): the output columns come in
+//    128-wide head groups [q0 gate0 q1 gate1 .. | k0 k1 .. | v0 v1 ..]; query and key groups
+//    are RMS-normalised (x * rsqrt(mean(x^2) + eps) * (1 + w)) and rotated in the epilogue,
+//    gate and value groups are stored as computed.  Rounding follows the eager ops: the
+//    projection is rounded, the norm computes in fp32 and rounds, and each rotary product and
+//    the sum are rounded.
+//
+// Tiles: 128 rows of h x 256 rows of W (two 128-row TMA boxes: gate rows j0.. and up rows
+// I + j0.. for SwiGLU, rows n0.. and n0 + 128.. otherwise).  K advances in 64-element
+// (128-byte) blocks: per block TMA loads a 16 KB h tile and the two 16 KB W tiles into one
+// 4-stage ring; placed back to back, the W tiles form the 256-row K-major B operand.
+// Persistent CTAs (one per SM) walk the tiles with the output column tile innermost, so the
+// CTAs in flight share h rows through L2.
 //
 // Warp roles (320 threads):
 //   warp 0       TMA producer (one lane)
 //   warp 1       TMEM allocator + MMA issuer (converged warp, one elected lane issues);
 //                accumulators double-buffered in TMEM columns [0, 256) and [256, 512)
-//   warps 2..9   epilogue: warp w reads TMEM lane quarter w % 4 (32 rows) and one half of
-//                the 128 output columns; its stores overlap the next tile's MMAs
+//   warps 2..9   epilogue: warp w reads TMEM lane quarter w % 4 (32 rows) and one 128-column
+//                half of the accumulator; its stores overlap the next tile's MMAs
 // Every wait is bounded: a timeout sets the CTA abort flag and the device error word, the
 // roles wind down, in-flight copies and MMAs are drained (again with bounded waits) and the
 // TMEM is freed.
@@ -48,19 +60,158 @@ constexpr uint32_t kStageBytes = 3 * 16384;  // h tile, gate tile, up tile
 constexpr uint32_t kBarOff = kStages * kStageBytes;
 constexpr uint32_t kGemmSmem = kBarOff + 256 + 1024;  // + barriers, + 1024-byte alignment slack
 
-struct SwigluGemmArgs {
-  int M, K, I;
+enum { kEpiSwiglu = 0, kEpiQKNorm = 1 };
+
+struct GemmArgs {
+  int M, K;
   int tiles_n, total_tiles;
+  int b2;        // W row offset of the second 128-row box of a tile (I for SwiGLU, 128 otherwise)
+  int tile_w;    // W rows a tile advances by (128 for SwiGLU, 256 otherwise)
   uint8_t* out;
-  int64_t ldo;  // elements
-  int st256;    // output base and row stride allow 32-byte stores
+  int64_t ldo;   // elements
+  int st256;     // output base and row stride allow 32-byte stores
   int* err;
+  // q/k norm + RoPE epilogue
+  int q_groups;  // head groups [0, q_groups) alternate query / gate
+  int k_groups;  // then k_groups key groups; the rest are values
+  const uint8_t* qn_w;
+  const uint8_t* kn_w;
+  const uint8_t* cs;  // cos / sin of row m at cs + 2 * m * rot (rot values each)
+  const uint8_t* sn;
+  int rot;
+  float eps;
 };
 
+__device__ __forceinline__ void unpack8v(const uint4& u, float* f, bool bf) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 t = bf ? ElemTraits<__nv_bfloat16>::unpack2(w[e]) : ElemTraits<__half>::unpack2(w[e]);
+    f[2 * e] = t.x;
+    f[2 * e + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ void store32(uint8_t* p, const uint32_t* w, bool st256) {
+  if (st256) {
+    st_256(p, w);
+  } else {
+    st_128(p, make_uint4(w[0], w[1], w[2], w[3]));
+    st_128(p + 16, make_uint4(w[4], w[5], w[6], w[7]));
+  }
+}
+
+// Normalised value of one rounded projection element: round(x * r * (1 + w)).
 template <typename T>
+__device__ __forceinline__ float qk_norm1(float x, float r, float w) {
+  return round_to<T>((round_to<T>(x) * r) * (1.f + w));
+}
+
+// Epilogue of one 128-column head group of the q/k/v projection for this thread's row:
+// `kind` 0 stores the rounded products, 1 / 2 normalises them (query / key norm weights)
+// and rotates the first `rot` dims.  TMEM is read 32 columns per wait; stores are 32 bytes
+// per thread (one full sector of the row).
+template <typename T>
+__device__ __forceinline__ void qkv_group_epilogue(const GemmArgs& a, uint32_t tg, uint8_t* orow, bool store,
+                                                   int kind, int64_t m) {
+  using namespace sm100;
+  constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
+  const bool s256 = a.st256 != 0;
+  if (kind == 0) {
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 32) {
+      float x[32];
+      tmem_ld16(tg + (uint32_t)c, x);
+      tmem_ld16(tg + (uint32_t)(c + 16), x + 16);
+      tmem_ld_wait();
+      uint32_t w[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) w[e] = ElemTraits<T>::pack2(x[2 * e], x[2 * e + 1]);
+      if (store) {
+        store32(orow + 2 * c, w, s256);
+        store32(orow + 2 * c + 32, w + 8, s256);
+      }
+    }
+    return;
+  }
+  const uint8_t* wn = kind == 1 ? a.qn_w : a.kn_w;
+  // pass 1: sum of squares of the rounded projection
+  float ss = 0.f;
+#pragma unroll 1
+  for (int c = 0; c < 128; c += 32) {
+    float x[32];
+    tmem_ld16(tg + (uint32_t)c, x);
+    tmem_ld16(tg + (uint32_t)(c + 16), x + 16);
+    tmem_ld_wait();
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const float v = round_to<T>(x[e]);
+      ss = fmaf(v, v, ss);
+    }
+  }
+  const float r = rsqrtf(ss * (1.f / 128.f) + a.eps);
+  const int hr = a.rot >> 1;
+  const uint8_t* csr = a.cs + 2 * m * a.rot;
+  const uint8_t* snr = a.sn + 2 * m * a.rot;
+  // pass 2a: rotary dims, in pairs of 16-column chunks (d, d + rot/2)
+#pragma unroll 1
+  for (int c = 0; c < hr; c += 16) {
+    float x1[16], x2[16];
+    tmem_ld16(tg + (uint32_t)c, x1);
+    tmem_ld16(tg + (uint32_t)(c + hr), x2);
+    tmem_ld_wait();
+    uint32_t o1[8], o2[8];
+#pragma unroll
+    for (int hb = 0; hb < 16; hb += 8) {
+      float w1[8], w2[8], c1[8], c2[8], s1[8], s2[8];
+      unpack8v(ld_nc_128(wn + 2 * (c + hb)), w1, bf);
+      unpack8v(ld_nc_128(wn + 2 * (c + hr + hb)), w2, bf);
+      unpack8v(ld_nc_128(csr + 2 * (c + hb)), c1, bf);
+      unpack8v(ld_nc_128(csr + 2 * (c + hr + hb)), c2, bf);
+      unpack8v(ld_nc_128(snr + 2 * (c + hb)), s1, bf);
+      unpack8v(ld_nc_128(snr + 2 * (c + hr + hb)), s2, bf);
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        float y1[2], y2[2];
+#pragma unroll
+        for (int f = 0; f < 2; ++f) {
+          const float n1 = qk_norm1<T>(x1[hb + e + f], r, w1[e + f]);
+          const float n2 = qk_norm1<T>(x2[hb + e + f], r, w2[e + f]);
+          y1[f] = round_to<T>(round_to<T>(n1 * c1[e + f]) + round_to<T>(-n2 * s1[e + f]));
+          y2[f] = round_to<T>(round_to<T>(n2 * c2[e + f]) + round_to<T>(n1 * s2[e + f]));
+        }
+        o1[(hb + e) >> 1] = ElemTraits<T>::pack2(y1[0], y1[1]);
+        o2[(hb + e) >> 1] = ElemTraits<T>::pack2(y2[0], y2[1]);
+      }
+    }
+    if (store) {
+      store32(orow + 2 * c, o1, s256);
+      store32(orow + 2 * (c + hr), o2, s256);
+    }
+  }
+  // pass 2b: the remaining dims, normalised only
+#pragma unroll 1
+  for (int c = a.rot; c < 128; c += 16) {
+    float x[16];
+    tmem_ld16(tg + (uint32_t)c, x);
+    tmem_ld_wait();
+    uint32_t o[8];
+#pragma unroll
+    for (int hb = 0; hb < 16; hb += 8) {
+      float w[8];
+      unpack8v(ld_nc_128(wn + 2 * (c + hb)), w, bf);
+#pragma unroll
+      for (int e = 0; e < 8; e += 2)
+        o[(hb + e) >> 1] = ElemTraits<T>::pack2(qk_norm1<T>(x[hb + e], r, w[e]), qk_norm1<T>(x[hb + e + 1], r, w[e + 1]));
+    }
+    if (store) store32(orow + 2 * c, o, s256);
+  }
+}
+
+template <typename T, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_swiglu_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                       const __grid_constant__ SwigluGemmArgs a) {
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                      const __grid_constant__ GemmArgs a) {
   using namespace sm100;
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -108,7 +259,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       int it = 0;
       for (int tile = blockIdx.x; tile < a.total_tiles && !*abort_flag; tile += gridDim.x) {
-        const int m0 = (tile / a.tiles_n) * 128, j0 = (tile % a.tiles_n) * 128;
+        const int m0 = (tile / a.tiles_n) * 128, j0 = (tile % a.tiles_n) * a.tile_w;
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % kStages, use = it / kStages;
@@ -120,7 +271,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           mbar_arrive_expect_tx(&full[s], kStageBytes);
           tma_load_4d(st, &tmA, &full[s], kb * 64, m0, 0, 0);
           tma_load_4d(st + 16384, &tmW, &full[s], kb * 64, j0, 0, 0);
-          tma_load_4d(st + 32768, &tmW, &full[s], kb * 64, a.I + j0, 0, 0);
+          tma_load_4d(st + 32768, &tmW, &full[s], kb * 64, a.b2 + j0, 0, 0);
         }
         if (!ok) break;
       }
@@ -175,31 +326,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int buf = tc & 1;
       if (!mbar_wait(&accfull[buf], (uint32_t)(tc >> 1) & 1u, abort_flag, 25, a.err)) break;
       tc_fence_after();
-      const int m = (tile / a.tiles_n) * 128 + row, j0 = (tile % a.tiles_n) * 128;
+      const int m = (tile / a.tiles_n) * 128 + row, tn = tile % a.tiles_n;
       const uint32_t tacc = tmem + lane_off + (uint32_t)buf * 256u;
-      uint8_t* orow = a.out + 2 * ((int64_t)m * a.ldo + j0);
+      if constexpr (EPI == kEpiSwiglu) {
+        uint8_t* orow = a.out + 2 * ((int64_t)m * a.ldo + tn * 128);
 #pragma unroll 1
-      for (int c = half * 64; c < half * 64 + 64; c += 16) {
-        float g[16], u[16];
-        tmem_ld16(tacc + (uint32_t)c, g);
-        tmem_ld16(tacc + 128u + (uint32_t)c, u);
-        tmem_ld_wait();
-        uint32_t w[8];
+        for (int c = half * 64; c < half * 64 + 64; c += 16) {
+          float g[16], u[16];
+          tmem_ld16(tacc + (uint32_t)c, g);
+          tmem_ld16(tacc + 128u + (uint32_t)c, u);
+          tmem_ld_wait();
+          uint32_t w[8];
 #pragma unroll
-        for (int e = 0; e < 16; e += 2) {
-          const float g0 = round_to<T>(g[e]), g1 = round_to<T>(g[e + 1]);
-          const float s0 = round_to<T>(g0 / (1.f + __expf(-g0))), s1 = round_to<T>(g1 / (1.f + __expf(-g1)));
-          w[e >> 1] = ElemTraits<T>::mul2(ElemTraits<T>::pack2(s0, s1),
-                                          ElemTraits<T>::pack2(u[e], u[e + 1]));
-        }
-        if (m < a.M) {
-          if (a.st256) {
-            st_256(orow + 2 * c, w);
-          } else {
-            st_128(orow + 2 * c, make_uint4(w[0], w[1], w[2], w[3]));
-            st_128(orow + 2 * c + 16, make_uint4(w[4], w[5], w[6], w[7]));
+          for (int e = 0; e < 16; e += 2) {
+            const float g0 = round_to<T>(g[e]), g1 = round_to<T>(g[e + 1]);
+            const float s0 = round_to<T>(g0 / (1.f + __expf(-g0))), s1 = round_to<T>(g1 / (1.f + __expf(-g1)));
+            w[e >> 1] = ElemTraits<T>::mul2(ElemTraits<T>::pack2(s0, s1),
+                                            ElemTraits<T>::pack2(u[e], u[e + 1]));
+          }
+          if (m < a.M) {
+            if (a.st256) {
+              st_256(orow + 2 * c, w);
+            } else {
+              st_128(orow + 2 * c, make_uint4(w[0], w[1], w[2], w[3]));
+              st_128(orow + 2 * c + 16, make_uint4(w[4], w[5], w[6], w[7]));
+            }
           }
         }
+      } else {
+        const int grp = tn * 2 + half;  // 128-column head group of this warp
+        const int kind = grp < a.q_groups ? ((grp & 1) ? 0 : 1) : (grp < a.q_groups + a.k_groups ? 2 : 0);
+        qkv_group_epilogue<T>(a, tacc + (uint32_t)half * 128u, a.out + 2 * ((int64_t)m * a.ldo + grp * 128),
+                              m < a.M, kind, m < a.M ? m : 0);
       }
       tc_fence_before();
       __syncwarp();
@@ -262,33 +420,10 @@ int sm_count(int dev) {
 
 using namespace bna;
 
-extern "C" BNA_API int bna_gemm_swiglu(const void* h, int64_t ldh, const void* w, int64_t ldw, void* out, int64_t ldo,
-                                       int64_t M, int32_t K, int32_t inter, int32_t dtype, void* stream) {
-  if (dtype != BNA_BF16 && dtype != BNA_F16) return fail(BNA_BAD_DTYPE, "gemm_swiglu: bfloat16 or float16 only");
-  if (M < 0 || K <= 0 || inter <= 0) return fail(BNA_BAD_SHAPE, "gemm_swiglu: bad sizes");
-  if (M == 0) return BNA_OK;
-  if (!h || !w || !out) return fail(BNA_BAD_SHAPE, "gemm_swiglu: null pointer");
-  if (K % 64 || inter % 128) return fail(BNA_UNSUPPORTED, "gemm_swiglu: K must be a multiple of 64, inter of 128");
-  if (ldh < K || ldw < K || ldo < inter) return fail(BNA_BAD_STRIDE, "gemm_swiglu: row strides below the row length");
-  if (ldh % 8 || ldw % 8 || ldo % 8) return fail(BNA_BAD_STRIDE, "gemm_swiglu: row strides must be multiples of 8 elements");
-  if ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out)) & 15)
-    return fail(BNA_BAD_STRIDE, "gemm_swiglu: pointers must be 16-byte aligned");
-  if (M >= ((int64_t)1 << 31) - 128) return fail(BNA_UNSUPPORTED, "gemm_swiglu: too many rows");
-  const CUtensorMapDataType dt = dtype == BNA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUtensorMap ma, mw;
-  if (int rc = encode_rows(&ma, h, M, K, ldh, dt, "h")) return rc;
-  if (int rc = encode_rows(&mw, w, 2 * (int64_t)inter, K, ldw, dt, "w")) return rc;
-  SwigluGemmArgs a{};
-  a.M = (int)M;
-  a.K = K;
-  a.I = inter;
-  a.tiles_n = inter / 128;
-  const int64_t tiles = ((M + 127) / 128) * a.tiles_n;
-  if (tiles >= ((int64_t)1 << 31)) return fail(BNA_UNSUPPORTED, "gemm_swiglu: too many tiles");
-  a.total_tiles = (int)tiles;
-  a.out = static_cast<uint8_t*>(out);
-  a.ldo = ldo;
-  a.st256 = ((reinterpret_cast<uintptr_t>(out) & 31) == 0 && (ldo * 2) % 32 == 0) ? 1 : 0;
+namespace bna {
+namespace {
+
+int launch_gemm(int epi, const CUtensorMap& ma, const CUtensorMap& mw, GemmArgs& a, int dtype, void* stream) {
   a.err = device_error_word();
   int dev = 0;
   cudaGetDevice(&dev);
@@ -317,7 +452,91 @@ extern "C" BNA_API int bna_gemm_swiglu(const void* h, int64_t ldh, const void* w
     cfg.numAttrs = 1;
     cudaLaunchKernelEx(&cfg, kern, ma, mw, a);
   };
-  if (dtype == BNA_BF16) launch(gemm_swiglu_kernel<__nv_bfloat16>);
-  else launch(gemm_swiglu_kernel<__half>);
-  return check_cuda(cudaGetLastError(), "gemm_swiglu launch");
+  const bool bf = dtype == BNA_BF16;
+  if (epi == kEpiSwiglu) bf ? launch(gemm_sm100_kernel<__nv_bfloat16, kEpiSwiglu>) : launch(gemm_sm100_kernel<__half, kEpiSwiglu>);
+  else bf ? launch(gemm_sm100_kernel<__nv_bfloat16, kEpiQKNorm>) : launch(gemm_sm100_kernel<__half, kEpiQKNorm>);
+  return check_cuda(cudaGetLastError(), "gemm_sm100 launch");
+}
+
+int check_gemm_common(const void* h, int64_t ldh, const void* w, int64_t ldw, const void* out, int64_t ldo, int64_t M,
+                      int32_t K, int32_t dtype, const char* name) {
+  const std::string n(name);
+  if (dtype != BNA_BF16 && dtype != BNA_F16) return fail(BNA_BAD_DTYPE, n + ": bfloat16 or float16 only");
+  if (M < 0 || K <= 0) return fail(BNA_BAD_SHAPE, n + ": bad sizes");
+  if (M > 0 && (!h || !w || !out)) return fail(BNA_BAD_SHAPE, n + ": null pointer");
+  if (K % 64) return fail(BNA_UNSUPPORTED, n + ": K must be a multiple of 64");
+  if (ldh < K || ldw < K) return fail(BNA_BAD_STRIDE, n + ": row strides below the row length");
+  if (ldh % 8 || ldw % 8 || ldo % 8) return fail(BNA_BAD_STRIDE, n + ": row strides must be multiples of 8 elements");
+  if ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(BNA_BAD_STRIDE, n + ": pointers must be 16-byte aligned");
+  if (M >= ((int64_t)1 << 31) - 128) return fail(BNA_UNSUPPORTED, n + ": too many rows");
+  return BNA_OK;
+}
+
+}  // namespace
+}  // namespace bna
+
+extern "C" BNA_API int bna_gemm_swiglu(const void* h, int64_t ldh, const void* w, int64_t ldw, void* out, int64_t ldo,
+                                       int64_t M, int32_t K, int32_t inter, int32_t dtype, void* stream) {
+  if (int rc = check_gemm_common(h, ldh, w, ldw, out, ldo, M, K, dtype, "gemm_swiglu")) return rc;
+  if (inter <= 0 || inter % 128) return fail(BNA_UNSUPPORTED, "gemm_swiglu: inter must be a positive multiple of 128");
+  if (ldo < inter) return fail(BNA_BAD_STRIDE, "gemm_swiglu: output row stride below inter");
+  if (M == 0) return BNA_OK;
+  const CUtensorMapDataType dt = dtype == BNA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ma, mw;
+  if (int rc = encode_rows(&ma, h, M, K, ldh, dt, "h")) return rc;
+  if (int rc = encode_rows(&mw, w, 2 * (int64_t)inter, K, ldw, dt, "w")) return rc;
+  GemmArgs a{};
+  a.M = (int)M;
+  a.K = K;
+  a.tiles_n = inter / 128;
+  a.total_tiles = (int)(((M + 127) / 128) * a.tiles_n);
+  a.b2 = inter;
+  a.tile_w = 128;
+  a.out = static_cast<uint8_t*>(out);
+  a.ldo = ldo;
+  a.st256 = ((reinterpret_cast<uintptr_t>(out) & 31) == 0 && (ldo * 2) % 32 == 0) ? 1 : 0;
+  return launch_gemm(kEpiSwiglu, ma, mw, a, dtype, stream);
+}
+
+extern "C" BNA_API int bna_gemm_qkv_norm_rope(const void* h, int64_t ldh, const void* w, int64_t ldw, void* out,
+                                              int64_t ldo, int64_t M, int32_t K, int32_t N, int32_t num_q_heads,
+                                              int32_t num_kv_heads, const void* q_norm_w, const void* k_norm_w,
+                                              const void* cos, const void* sin, int32_t rot, float eps, int32_t dtype,
+                                              void* stream) {
+  if (int rc = check_gemm_common(h, ldh, w, ldw, out, ldo, M, K, dtype, "gemm_qkv_norm_rope")) return rc;
+  if (N <= 0 || N % 256) return fail(BNA_UNSUPPORTED, "gemm_qkv_norm_rope: N must be a positive multiple of 256");
+  if (ldo < N) return fail(BNA_BAD_STRIDE, "gemm_qkv_norm_rope: output row stride below N");
+  if (num_q_heads <= 0 || num_kv_heads <= 0 || (2 * num_q_heads + 2 * num_kv_heads) * 128 != N)
+    return fail(BNA_BAD_SHAPE, "gemm_qkv_norm_rope: N must be (2 * q heads + 2 * kv heads) * 128");
+  if (rot < 0 || rot > 128 || rot % 32) return fail(BNA_UNSUPPORTED, "gemm_qkv_norm_rope: rot must be a multiple of 32 up to 128");
+  if (M > 0 && (!q_norm_w || !k_norm_w || (rot > 0 && (!cos || !sin))))
+    return fail(BNA_BAD_SHAPE, "gemm_qkv_norm_rope: null norm weights or rotary tables");
+  if ((reinterpret_cast<uintptr_t>(q_norm_w) | reinterpret_cast<uintptr_t>(k_norm_w) | reinterpret_cast<uintptr_t>(cos) |
+       reinterpret_cast<uintptr_t>(sin)) & 15)
+    return fail(BNA_BAD_STRIDE, "gemm_qkv_norm_rope: norm weights and rotary tables must be 16-byte aligned");
+  if (M == 0) return BNA_OK;
+  const CUtensorMapDataType dt = dtype == BNA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ma, mw;
+  if (int rc = encode_rows(&ma, h, M, K, ldh, dt, "h")) return rc;
+  if (int rc = encode_rows(&mw, w, N, K, ldw, dt, "w")) return rc;
+  GemmArgs a{};
+  a.M = (int)M;
+  a.K = K;
+  a.tiles_n = N / 256;
+  a.total_tiles = (int)(((M + 127) / 128) * a.tiles_n);
+  a.b2 = 128;
+  a.tile_w = 256;
+  a.out = static_cast<uint8_t*>(out);
+  a.ldo = ldo;
+  a.q_groups = 2 * num_q_heads;
+  a.k_groups = num_kv_heads;
+  a.qn_w = static_cast<const uint8_t*>(q_norm_w);
+  a.kn_w = static_cast<const uint8_t*>(k_norm_w);
+  a.cs = static_cast<const uint8_t*>(cos);
+  a.sn = static_cast<const uint8_t*>(sin);
+  a.rot = rot;
+  a.eps = eps;
+  a.st256 = ((reinterpret_cast<uintptr_t>(out) & 31) == 0 && (ldo * 2) % 32 == 0) ? 1 : 0;
+  return launch_gemm(kEpiQKNorm, ma, mw, a, dtype, stream);
 }

@@ -165,6 +165,34 @@ def gemm_swiglu(h: torch.Tensor, w_gate_up: torch.Tensor, inter: int) -> torch.T
     return out
 
 
+def gemm_qkv_norm_rope(h: torch.Tensor, w_qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int,
+                       q_weight: torch.Tensor, k_weight: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                       eps: float) -> torch.Tensor:
+    """h [B,T,K] @ w_qkv^T on the tcgen05 GEMM, w_qkv [N, K] the merged gated q_proj, k_proj and
+    v_proj rows (per query head 128 query then 128 gate rows; N = (2 Hq + 2 Hkv) * 128), with
+    the q/k RMSNorm and the rotary embedding (cos/sin [B,T,rot] or [1,T,rot]) applied to the
+    query and key columns in the epilogue -> [B,T,N] (the layout the projection had)."""
+    _lib.require_cuda(h, w_qkv, q_weight, k_weight, cos, sin)
+    B, T, K = h.shape
+    N = int(w_qkv.shape[0])
+    rows, ldh = _rows(h, K)
+    if w_qkv.dim() != 2 or int(w_qkv.shape[1]) != K or w_qkv.stride(1) != 1 or w_qkv.dtype != h.dtype:
+        raise ValueError("w_qkv must be a row-major [N, K] matrix of h's dtype")
+    rot = int(cos.shape[-1])
+    cs = cos.reshape(B * T, rot) if cos.shape[0] == B else cos.expand(B, T, rot).reshape(B * T, rot)
+    sn = sin.reshape(B * T, rot) if sin.shape[0] == B else sin.expand(B, T, rot).reshape(B * T, rot)
+    cs, sn = cs.to(h.dtype).contiguous(), sn.to(h.dtype).contiguous()
+    for w in (q_weight, k_weight):
+        if w.dtype != h.dtype or w.numel() != 128 or not w.is_contiguous():
+            raise ValueError("norm weights must be contiguous [128] tensors of h's dtype")
+    out = torch.empty((B, T, N), device=h.device, dtype=h.dtype)
+    _lib.check(_lib.lib().bna_gemm_qkv_norm_rope(
+        h.data_ptr(), ldh, w_qkv.data_ptr(), w_qkv.stride(0), out.data_ptr(), N, rows, K, N, int(num_q_heads),
+        int(num_kv_heads), q_weight.data_ptr(), k_weight.data_ptr(), cs.data_ptr(), sn.data_ptr(), rot, float(eps),
+        _lib.dtype_code(h.dtype), _lib.stream_ptr(h.device)))
+    return out
+
+
 def _mat(x: torch.Tensor, K: int) -> tuple[int, int]:
     """(tokens, row stride) of a [M, K] matrix view with a contiguous last dim."""
     if x.dim() != 2 or x.shape[1] != K or x.stride(1) != 1:

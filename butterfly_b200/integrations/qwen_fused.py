@@ -7,8 +7,8 @@ rotary-embedding concatenations, separate sigmoid / SiLU / multiply / residual p
 ``fuse_qwen_decoder_layers`` replaces that glue, per swapped layer, with:
 
     h   = rmsnorm(x)                                  one kernel   (input_layernorm)
-    qkv = h @ [Wq; Wk; Wv]^T                          one GEMM     (q/k/v projections merged)
-    q,k = qk_norm_rope(q part, k part)                one kernel   (q_norm/k_norm + partial RoPE)
+    qkv = h @ [Wq; Wk; Wv]^T, q/k norm + RoPE         one tcgen05 GEMM (q/k/v merged; q_norm/k_norm
+                                                      and the partial RoPE in its epilogue)
     y   = attention(q,k,v) * sigmoid(gate)            the path's kernels (whole-prompt prefill: the
                                                       gate is applied in the attention kernel's store;
                                                       otherwise one more kernel)
@@ -77,6 +77,9 @@ class _FusedState:
         self.inter = mlp.gate_proj.out_features
         # the tcgen05 gate/up GEMM tiles K by 64 and the intermediate size by 128
         self.gemm_swiglu = mlp.gate_proj.in_features % 64 == 0 and self.inter % 128 == 0
+        # and the q/k/v GEMM with the q/k norm + RoPE epilogue: 128-wide heads, N by 256
+        self.gemm_qkv = (src.q_proj.in_features % 64 == 0 and self.dh == 128 and
+                         int(self.w_qkv.shape[0]) % 256 == 0)
 
 
 def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=None, attention_mask=None,
@@ -98,14 +101,20 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
     if decode:  # weight-streaming projections with the norms, gate and residual adds fused in
         qkv = glue.gemv_rmsnorm(x.view(B, H), self.input_layernorm.weight, self.input_layernorm.eps,
                                 st.w_qkv).view(B, 1, -1)
-    else:
+    cos, sin = position_embeddings
+    # whole-prompt / chunk prefill: q/k norm + RoPE in the q/k/v GEMM's epilogue
+    prepped = (not decode and attn._shard is None and st.gemm_qkv and int(cos.shape[-1]) % 32 == 0)
+    if not decode:
         h = glue.rmsnorm(x, self.input_layernorm.weight, self.input_layernorm.eps)
-        qkv = F.linear(h, st.w_qkv)                               # [B,T,2*hq*dh + 2*hkv*dh]
+        if prepped:
+            qkv = glue.gemm_qkv_norm_rope(h, st.w_qkv, hq, hkv, src.q_norm.weight, src.k_norm.weight, cos, sin,
+                                          src.q_norm.eps)
+        else:
+            qkv = F.linear(h, st.w_qkv)                           # [B,T,2*hq*dh + 2*hkv*dh]
     nq = 2 * hq * dh
     qg = qkv[..., :nq].view(B, T, hq, 2 * dh)                     # per head: query, then gate
     k_raw = qkv[..., nq:nq + hkv * dh].view(B, T, hkv, dh)
     v = qkv[..., nq + hkv * dh:].view(B, T, hkv, dh)
-    cos, sin = position_embeddings
     gated = None  # the gated attention output [B,T,hq*dh] when the gate rode along with attention
     if attn._shard is not None:
         # sequence shard: K and V go straight into buffers whose first W-1 rows receive the
@@ -122,8 +131,11 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
         out, backend, hit = attn.attend(qg[..., :dh].transpose(1, 2), k_raw.transpose(1, 2), v.transpose(1, 2),
                                         comp_cache, cache_len, k_len_after, qk_prep=prep)
     else:
-        q, k = glue.qk_norm_rope(qg[..., :dh], k_raw, src.q_norm.weight, src.k_norm.weight, cos, sin,
-                                 src.q_norm.eps)
+        if prepped:
+            q, k = qg[..., :dh], k_raw
+        else:
+            q, k = glue.qk_norm_rope(qg[..., :dh], k_raw, src.q_norm.weight, src.k_norm.weight, cos, sin,
+                                     src.q_norm.eps)
         qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
         if comp_cache is None and past_key_values is not None:
             kt, vt = past_key_values.update(kt, vt, attn.layer_idx)

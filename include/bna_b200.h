@@ -254,6 +254,19 @@ BNA_API int bna_swiglu(const void* gate_up, int64_t row_stride, int64_t up_offse
 BNA_API int bna_gemm_swiglu(const void* h, int64_t ldh, const void* w, int64_t ldw, void* out, int64_t ldo,
                             int64_t M, int32_t K, int32_t inter, int32_t dtype, void* stream);
 
+/* The merged q/k/v projection with the q/k RMSNorm and rotary embedding in the epilogue:
+ * out[m, :] = h[m,:] . w^T for w [N, K] whose rows come in 128-row head groups
+ * [q0 gate0 q1 gate1 .. q(Hq-1) gate(Hq-1) | k0 .. k(Hkv-1) | v0 .. v(Hkv-1)]
+ * (N = (2 Hq + 2 Hkv) * 128, a multiple of 256); every query and key group is then
+ * normalised (Qwen3.5 RMSNorm, weights q_norm_w / k_norm_w [128]) and rotated in
+ * rotate-half form on its first `rot` dims with cos / sin [M, rot] (row m's tables),
+ * the rounding steps of the eager ops (bna_qk_norm_rope); gate and value groups are the
+ * rounded products.  K a multiple of 64, rot a multiple of 32. */
+BNA_API int bna_gemm_qkv_norm_rope(const void* h, int64_t ldh, const void* w, int64_t ldw, void* out, int64_t ldo,
+                                   int64_t M, int32_t K, int32_t N, int32_t num_q_heads, int32_t num_kv_heads,
+                                   const void* q_norm_w, const void* k_norm_w, const void* cos, const void* sin,
+                                   int32_t rot, float eps, int32_t dtype, void* stream);
+
 /* Decode-time projections for 1..8 tokens (y = W x per token, W [out_features,
  * in_features] row-major, in_features a multiple of 256), with the layer step before the
  * projection fused in front of it and the one after it fused behind it.  Replace the

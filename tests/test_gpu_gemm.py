@@ -56,3 +56,34 @@ def test_gemm_swiglu_rejects_bad_shapes():
     w = torch.randn(256, 100, device="cuda").bfloat16()
     with pytest.raises(Exception):
         glue.gemm_swiglu(h, w, 128)  # K not a multiple of 64
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,T,K,Hq,Hkv,rot", [(1, 1000, 1024, 8, 2, 32), (2, 300, 2560, 16, 4, 64), (1, 70, 1024, 8, 2, 128)])
+def test_gemm_qkv_norm_rope_matches_unfused(dtype, B, T, K, Hq, Hkv, rot):
+    """The q/k/v GEMM with the q/k norm + RoPE epilogue against cuBLAS + bna_qk_norm_rope."""
+    g = torch.Generator(device="cuda").manual_seed(T + K)
+    dh = 128
+    N = (2 * Hq + 2 * Hkv) * dh
+    h = torch.randn(B, T, K, device="cuda", generator=g).to(dtype)
+    w = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).to(dtype)
+    qw = (torch.randn(dh, device="cuda", generator=g) * 0.1).to(dtype)
+    kw = (torch.randn(dh, device="cuda", generator=g) * 0.1).to(dtype)
+    pos = torch.arange(T, device="cuda", dtype=torch.float32) + 5
+    inv = 1.0 / (10000 ** (torch.arange(0, rot, 2, device="cuda", dtype=torch.float32) / rot))
+    fr = torch.cat([pos[:, None] * inv[None], pos[:, None] * inv[None]], -1)
+    cos, sin = fr.cos()[None].to(dtype), fr.sin()[None].to(dtype)
+    got = glue.gemm_qkv_norm_rope(h, w, Hq, Hkv, qw, kw, cos, sin, 1e-6)
+    ref = F.linear(h, w)
+    nq = 2 * Hq * dh
+    qg = ref[..., :nq].view(B, T, Hq, 2 * dh)
+    q_ref, k_ref = glue.qk_norm_rope(qg[..., :dh], ref[..., nq:nq + Hkv * dh].view(B, T, Hkv, dh), qw, kw, cos, sin,
+                                     1e-6)
+    gg = got[..., :nq].view(B, T, Hq, 2 * dh)
+    pairs = [(gg[..., :dh], q_ref), (got[..., nq:nq + Hkv * dh].view(B, T, Hkv, dh), k_ref),
+             (gg[..., dh:], qg[..., dh:]), (got[..., nq + Hkv * dh:], ref[..., nq + Hkv * dh:])]
+    for a, b in pairs:
+        a, b = a.float(), b.float()
+        scale = float(b.abs().max())
+        assert float((a - b).abs().max()) <= 0.03 * scale
+        assert float((a == b).float().mean()) >= 0.85
