@@ -354,11 +354,11 @@ def run_model(args, ws, rank, local, dev, peaks):
                      "flops_per_step": flops,
                      "flops_note": "2 x linear MACs per token (352.3M non-embedding params) + attention over "
                                    "selected keys + lm_head for the kept position; per GPU",
-                     "traffic_note": "the step's dominant kernels are cuBLAS GEMMs; DRAM traffic is given for "
+                     "traffic_note": "the step's dominant kernels are GEMMs (ours for q/k/v and gate/up, cuBLAS for o/down); DRAM traffic is given for "
                                      "the attention kernel below",
                      "attention_kernel": att},
         "decode": decode,
-        "launches_per_step": 8 * MODEL["layers"] + 1,
+        "launches_per_step": 7 * MODEL["layers"] + 1,
     }
 
 
@@ -1105,6 +1105,23 @@ def profile_case(kind: str):
         mb.prefill()
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_pop()
+    elif kind in ("gemm-swiglu", "gemm-qkv"):
+        # the model's gate/up (or q/k/v) projection at T=131072: 3 warm-up launches, then one
+        from butterfly_b200 import glue
+        g = torch.Generator(device=dev).manual_seed(0)
+        H = MODEL["hidden"]
+        h = torch.randn(1, MODEL_T, H, device=dev, generator=g).bfloat16()
+        if kind == "gemm-swiglu":
+            w = (torch.randn(2 * MODEL["inter"], H, device=dev, generator=g) / H ** 0.5).bfloat16()
+            fn = lambda: glue.gemm_swiglu(h, w, MODEL["inter"])  # noqa: E731
+        else:
+            hq, hkv, dh = MODEL["heads"], MODEL["kv_heads"], MODEL["head_dim"]
+            w = (torch.randn((2 * hq + 2 * hkv) * dh, H, device=dev, generator=g) / H ** 0.5).bfloat16()
+            nw = torch.ones(dh, device=dev, dtype=torch.bfloat16)
+            cs = torch.randn(1, MODEL_T, 32, device=dev, generator=g).bfloat16()
+            fn = lambda: glue.gemm_qkv_norm_rope(h, w, hq, hkv, nw, nw, cs, cs, 1e-6)  # noqa: E731
+        for _ in range(4):
+            fn()
     else:
         run_decode(dev, 0, reps=1, warmup=1)
     torch.cuda.synchronize()
@@ -1122,7 +1139,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the batched-decode leg")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-shard", action="store_true", help="skip the sequence-sharded 262k leg")
-    ap.add_argument("--profile-case", choices=["prefill", "decode", "prefill-trace", "model-prefill", "model-decode", "prefill-128k"], default=None,
+    ap.add_argument("--profile-case", choices=["prefill", "decode", "prefill-trace", "model-prefill", "model-decode", "prefill-128k",
+                                                      "gemm-swiglu", "gemm-qkv"], default=None,
                     help="small case for ncu: warm-up, then the launches to capture")
     args = ap.parse_args()
     if args.profile_case:
@@ -1162,9 +1180,9 @@ def main():
         "cpu_baseline": cpu,
         "e2e": m["e2e"],
         "gpu_launches": args.steps * m["launches_per_step"],
-        "gpu_launches_note": "our kernels per prefill: per layer input RMSNorm, q/k norm+RoPE, compressor, prefill "
-                             "kernel, cache hand-off append, sigmoid gate, residual+RMSNorm, SwiGLU (8), plus the "
-                             "final norm",
+        "gpu_launches_note": "our kernels per prefill: per layer input RMSNorm, q/k/v GEMM with q/k norm+RoPE, "
+                             "compressor, gated prefill kernel, cache hand-off append, residual+RMSNorm, gate/up "
+                             "GEMM with SwiGLU (7), plus the final norm; cuBLAS runs o_proj and down_proj",
         "timing": "CUDA events around the timed prefills; decode from CUDA-graph replays",
         "clocks": m["clocks"],
         "decode": m["decode"],
