@@ -80,6 +80,40 @@ def test_decode_step_qk_rejections():
     assert L().bna_decode_step_qk(*args_bad, 32, 1e-6, None) == BAD_SHAPE
 
 
+def test_gemm_rejections():
+    sw = L().bna_gemm_swiglu
+    assert sw(P, 1024, P, 1024, P, 3584, 0, 1024, 3584, BF, None) == OK          # no rows: no launch
+    assert sw(P, 1024, P, 1024, P, 3584, 8, 1000, 3584, BF, None) == UNSUPPORTED  # K % 64
+    assert sw(P, 1024, P, 1024, P, 3584, 8, 1024, 3500, BF, None) == UNSUPPORTED  # inter % 128
+    assert sw(P, 1024, P, 1024, P, 3584, 8, 1024, 3584, 7, None) == BAD_DTYPE
+    assert sw(P + 2, 1024, P, 1024, P, 3584, 8, 1024, 3584, BF, None) == BAD_STRIDE
+    assert sw(P, 1000, P, 1024, P, 3584, 8, 1024, 3584, BF, None) == BAD_STRIDE     # ldh < K
+    assert sw(None, 1024, P, 1024, P, 3584, 8, 1024, 3584, BF, None) == BAD_SHAPE
+    qk = L().bna_gemm_qkv_norm_rope
+
+    def q(**kw):
+        a = dict(h=P, ldh=1024, w=P, ldw=1024, out=P, ldo=2560, M=8, K=1024, N=2560, hq=8, hkv=2, qw=P, kw=P,
+                 cos=P, sin=P, rot=32, eps=1e-6, dt=BF, s=None)
+        a.update(kw)
+        return qk(*a.values())
+
+    assert q(M=0) == OK
+    assert q(N=2304) == BAD_SHAPE       # not (2 Hq + 2 Hkv) * 128
+    assert q(N=2432) == UNSUPPORTED     # not a multiple of 256
+    assert q(rot=16) == UNSUPPORTED
+    assert q(qw=None) == BAD_SHAPE
+    assert q(cos=P + 8) == BAD_STRIDE
+    assert q(ldo=2048) == BAD_STRIDE
+
+
+def test_prefill_gated_rejects_null_gate():
+    t = _lib.Tensor4()
+    r = _lib.Route()
+    f = L().bna_prefill_attention_gated
+    assert f(ctypes.byref(t), ctypes.byref(t), ctypes.byref(t), ctypes.byref(t), ctypes.byref(t), None,
+             ctypes.byref(t), None, 0, 0, BF, ctypes.byref(r), 64, 0, 0, 1, 0.1, None) == BAD_SHAPE
+
+
 def test_python_wrappers_refuse_cpu_tensors():
     x = torch.zeros(2, 1024, dtype=torch.bfloat16)
     w = torch.zeros(1024, dtype=torch.bfloat16)
