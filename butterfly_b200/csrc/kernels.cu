@@ -239,8 +239,8 @@ __device__ __forceinline__ void ldmatrix_x4_trans(const void* smem_row, uint32_t
 
 // One CTA per (query index, b * Hkv) serves the G query heads of a KV head.
 //   1. loads: the raw window rows, the routed summary rows and the G query rows arrive in
-//      shared memory by cp.async in one round trip.  In a fused decode step the ring rows of
-//      positions <= p - 2 are requested before griddepcontrol.wait (under programmatic
+//      shared memory in one round trip.  In a fused decode step the ring rows of
+//      positions <= p - 2 are requested (bulk copies) before griddepcontrol.wait (under programmatic
 //      dependent launch, while the previous kernel of the stream finishes): only the
 //      immediately preceding kernel can still be running, and in a decode step the ring rows
 //      it may write are those of position p - 1 (the previous step's append) at most.
@@ -303,11 +303,30 @@ __global__ void __launch_bounds__(decode_threads(G)) decode_kernel(const ActiveA
   };
   int64_t lo = 0;
   int nraw = 0, idx_lo = 0, npre = 0;
-  if (fused && p0 >= 0) {
+  // The pre-wait rows arrive by untiled bulk copies (one 256-byte row per instruction,
+  // counted on pre_bar) instead of 16-byte cp.async: the few cp.async issued after the
+  // wait then do not queue behind ~2k outstanding requests of the prefetch.
+  __shared__ __align__(8) uint64_t pre_bar;
+  const bool pre = fused && p0 >= 0;
+  if (pre) {
     window_of(p0, lo, nraw, idx_lo);
     npre = (int)(p0 - 1 - lo);  // rows j < npre sit at positions <= p - 2
     npre = npre < 0 ? 0 : (npre > nraw ? nraw : npre);
-    issue_rows(lo, idx_lo, 0, npre, nraw);
+    if (threadIdx.x == 0) {
+      sm100::mbar_init(&pre_bar, 1);
+      sm100::fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) sm100::mbar_arrive_expect_tx(&pre_bar, (uint32_t)npre * 512u);
+#pragma unroll 1
+    for (int j = threadIdx.x; j < 2 * npre; j += NT) {
+      const int isv = j >= npre;
+      const int jj = isv ? j - npre : j;
+      int idx = idx_lo + jj;
+      if (a.ring > 0 && idx >= (int)a.ring) idx -= (int)a.ring;
+      sm100::bulk_copy_g2s(kv + (isv * maxk + jj) * kDecPitch, row_ptr(isv ? a.v : a.k, b, kvh, idx), 256u,
+                           &pre_bar);
+    }
   }
   // Launched with programmatic stream serialization: wait for the previous kernel of the
   // stream (and its memory) before touching anything it may write, then let the next
@@ -361,6 +380,13 @@ __global__ void __launch_bounds__(decode_threads(G)) decode_kernel(const ActiveA
     cp_async_16(kv + (isv * maxk + nraw + j) * kDecPitch + ch * 16, row_ptr(isv ? a.vs : a.ks, b, kvh, sel[1 + j]) + ch * 16);
   }
   cp_async_wait_all();
+  if (pre) {
+    // bounded wait for the bulk-copied rows: on a timeout record the failure (read back by
+    // bna_take_device_error) and carry on rather than spin
+    bool done = false;
+    for (int it = 0; it < (1 << 24) && !done; ++it) done = sm100::mbar_try_wait(&pre_bar, 0);
+    if (!done && threadIdx.x == 0) atomicCAS(&g_device_error, 0, 0x1000 | 13);
+  }
   __syncthreads();
   if (a.qk_prep) {
     // warp r normalises and rotates query row r (r < G) or, for r == G, the new key row
