@@ -201,8 +201,7 @@ __host__ __device__ constexpr int decode_part_floats(int G) {
 size_t decode_smem_bytes(int G, int window) {
   const int maxk = window + kMaxSummaries;
   return (size_t)2 * kDecPitch * ((maxk + 15) / 16 * 16) + (size_t)G * kDecPitch + sizeof(float) * (size_t)decode_part_floats(G) +
-         sizeof(float) * (size_t)(decode_threads(G) / 32) * G * 2 + sizeof(int) * (1 + kMaxSummaries) +
-         sizeof(float) * (size_t)G * (decode_threads(G) / 32 + 1);
+         sizeof(float) * (size_t)(decode_threads(G) / 32) * G * 2 + sizeof(int) * (1 + kMaxSummaries);
 }
 
 __device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc) {
@@ -244,13 +243,12 @@ __device__ __forceinline__ void ldmatrix_x4_trans(const void* smem_row, uint32_t
 //      dependent launch, while the previous kernel of the stream finishes): only the
 //      immediately preceding kernel can still be running, and in a decode step the ring rows
 //      it may write are those of position p - 1 (the previous step's append) at most.
-//   2. one pass per half-warp: the 2 NW half-warps take keys in turn; for each key the G
-//      scores are 16-lane reduced dot products (lane l holds dims 8 (l & 15) .. + 7) and an
-//      online softmax (exp2 domain) keeps each head's running max, sum and output columns
-//      in registers.
-//   3. the 2 NW (max, sum, output) partials of each head are merged once through shared
-//      memory (the online log-sum-exp merge): one thread per head computes the rescale
-//      factors, then one thread per (head, two columns) sums the partials.
+//   2. each warp takes 16-key tiles in turn: S = Q K^T and O += P V on tensor cores
+//      (mma.sync m16n8k16, the G heads as rows), with an online softmax (exp2 domain) that
+//      keeps each head's running max, sum and output columns in registers.
+//   3. the per-warp (max, sum, output) partials of each head are merged once through shared
+//      memory (the online log-sum-exp merge): one thread per (head, two columns) derives
+//      the rescale factors and sums the partials.
 // Optionally the CTA also closes one block into the summary pool and appends the new token
 // to the ring (fused decode step).
 template <typename T, int G>
@@ -544,38 +542,35 @@ __global__ void __launch_bounds__(decode_threads(G)) decode_kernel(const ActiveA
     }
   }
   __syncthreads();
-  // per head: the global max, each partial's rescale factor and the total sum, once
+  // merge: thread = (head, two columns).  Each thread derives its head's global max, the
+  // partials' rescale factors and the total sum itself (a few shared-memory reads and
+  // nact exp2 per thread), so no second barrier and no serial per-head phase
   constexpr int NP = NW;  // partials per head
-  float* coef = reinterpret_cast<float*>(sel + 1 + kMaxSummaries);  // [G][NP + 1]
   const int nact = ntiles < NW ? ntiles : NW;  // warps that saw keys
-  if (threadIdx.x < G) {
-    const int g = threadIdx.x;
-    float M = -INFINITY;
-    for (int w = 0; w < nact; ++w) M = fmaxf(M, ml[(w * G + g) * 2]);
-    float L = 0.f;
-    for (int w = 0; w < nact; ++w) {
-      const float mw = ml[(w * G + g) * 2];
-      const float cw = mw == -INFINITY ? 0.f : ex2_approx(mw - M);
-      coef[g * (NP + 1) + w] = cw;
-      L = fmaf(ml[(w * G + g) * 2 + 1], cw, L);
-    }
-    coef[g * (NP + 1) + NP] = L > 0.f ? 1.f / L : 0.f;
-    if (a.lse) a.lse[b * a.ls_b + (int64_t)(kvh * G + g) * a.ls_h + t] = (M + log2f(L)) * 0.6931471805599453f;
-  }
-  __syncthreads();
-  // merge: thread = (head, two columns)
 #pragma unroll 1
   for (int r = threadIdx.x; r < G * 64; r += NT) {
     const int g = r >> 6, c = (r & 63) * 2;
-    const float* cf = coef + g * (NP + 1);
-    float s0 = 0.f, s1 = 0.f;
-    for (int w = 0; w < nact; ++w) {
-      const float2 f = *reinterpret_cast<const float2*>(part + (w * G + g) * 128 + c);
-      s0 = fmaf(f.x, cf[w], s0);
-      s1 = fmaf(f.y, cf[w], s1);
+    float mw[NP];
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NP; ++w) {
+      mw[w] = w < nact ? ml[(w * G + g) * 2] : -INFINITY;
+      M = fmaxf(M, mw[w]);
     }
-    const float inv = cf[NP];
+    float L = 0.f, s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int w = 0; w < NP; ++w) {
+      if (w < nact) {
+        const float cw = mw[w] == -INFINITY ? 0.f : ex2_approx(mw[w] - M);
+        L = fmaf(ml[(w * G + g) * 2 + 1], cw, L);
+        const float2 f = *reinterpret_cast<const float2*>(part + (w * G + g) * 128 + c);
+        s0 = fmaf(f.x, cw, s0);
+        s1 = fmaf(f.y, cw, s1);
+      }
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
     *reinterpret_cast<uint32_t*>(row_ptr(a.out, b, kvh * G + g, t) + c * 2) = ElemTraits<T>::pack2(s0 * inv, s1 * inv);
+    if (a.lse && c == 0) a.lse[b * a.ls_b + (int64_t)(kvh * G + g) * a.ls_h + t] = (M + log2f(L)) * 0.6931471805599453f;
   }
 }
 
