@@ -58,7 +58,8 @@ constexpr int kGemmThreads = 320;
 constexpr int kStages = 4;
 constexpr uint32_t kStageBytes = 3 * 16384;  // h tile, gate tile, up tile
 constexpr uint32_t kBarOff = kStages * kStageBytes;
-constexpr uint32_t kGemmSmem = kBarOff + 256 + 1024;  // + barriers, + 1024-byte alignment slack
+constexpr uint32_t kNormOff = kBarOff + 256;          // q / k norm weights (2 x 128 16-bit values)
+constexpr uint32_t kGemmSmem = kNormOff + 512 + 1024;  // + 1024-byte alignment slack
 
 enum { kEpiSwiglu = 0, kEpiQKNorm = 1 };
 
@@ -113,7 +114,7 @@ __device__ __forceinline__ float qk_norm1(float x, float r, float w) {
 // per thread (one full sector of the row).
 template <typename T>
 __device__ __forceinline__ void qkv_group_epilogue(const GemmArgs& a, uint32_t tg, uint8_t* orow, bool store,
-                                                   int kind, int64_t m) {
+                                                   int kind, int64_t m, const uint8_t* norm_smem) {
   using namespace sm100;
   constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
   const bool s256 = a.st256 != 0;
@@ -134,7 +135,14 @@ __device__ __forceinline__ void qkv_group_epilogue(const GemmArgs& a, uint32_t t
     }
     return;
   }
-  const uint8_t* wn = kind == 1 ? a.qn_w : a.kn_w;
+  const uint8_t* wn = norm_smem + (kind == 1 ? 0 : 256);  // this kind's norm weights (shared memory)
+  const uint8_t* csr = a.cs + 2 * m * a.rot;
+  const uint8_t* snr = a.sn + 2 * m * a.rot;
+  // the row's rotary tables come into L1 while pass 1 runs
+  for (int off = 0; off < 2 * a.rot; off += 128) {
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(csr + off));
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(snr + off));
+  }
   // pass 1: sum of squares of the rounded projection
   float ss = 0.f;
 #pragma unroll 1
@@ -151,8 +159,6 @@ __device__ __forceinline__ void qkv_group_epilogue(const GemmArgs& a, uint32_t t
   }
   const float r = rsqrtf(ss * (1.f / 128.f) + a.eps);
   const int hr = a.rot >> 1;
-  const uint8_t* csr = a.cs + 2 * m * a.rot;
-  const uint8_t* snr = a.sn + 2 * m * a.rot;
   // pass 2a: rotary dims, in pairs of 16-column chunks (d, d + rot/2)
 #pragma unroll 1
   for (int c = 0; c < hr; c += 16) {
@@ -164,8 +170,8 @@ __device__ __forceinline__ void qkv_group_epilogue(const GemmArgs& a, uint32_t t
 #pragma unroll
     for (int hb = 0; hb < 16; hb += 8) {
       float w1[8], w2[8], c1[8], c2[8], s1[8], s2[8];
-      unpack8v(ld_nc_128(wn + 2 * (c + hb)), w1, bf);
-      unpack8v(ld_nc_128(wn + 2 * (c + hr + hb)), w2, bf);
+      unpack8v(*reinterpret_cast<const uint4*>(wn + 2 * (c + hb)), w1, bf);
+      unpack8v(*reinterpret_cast<const uint4*>(wn + 2 * (c + hr + hb)), w2, bf);
       unpack8v(ld_nc_128(csr + 2 * (c + hb)), c1, bf);
       unpack8v(ld_nc_128(csr + 2 * (c + hr + hb)), c2, bf);
       unpack8v(ld_nc_128(snr + 2 * (c + hb)), s1, bf);
@@ -199,7 +205,7 @@ __device__ __forceinline__ void qkv_group_epilogue(const GemmArgs& a, uint32_t t
 #pragma unroll
     for (int hb = 0; hb < 16; hb += 8) {
       float w[8];
-      unpack8v(ld_nc_128(wn + 2 * (c + hb)), w, bf);
+      unpack8v(*reinterpret_cast<const uint4*>(wn + 2 * (c + hb)), w, bf);
 #pragma unroll
       for (int e = 0; e < 8; e += 2)
         o[(hb + e) >> 1] = ElemTraits<T>::pack2(qk_norm1<T>(x[hb + e], r, w[e]), qk_norm1<T>(x[hb + e + 1], r, w[e + 1]));
@@ -247,6 +253,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmW);
+  }
+  if (EPI == kEpiQKNorm && warp == 2) {  // the q and k norm weights, once per CTA
+    const uint8_t* src = lane < 16 ? a.qn_w + 16 * lane : a.kn_w + 16 * (lane - 16);
+    *reinterpret_cast<uint4*>(smem + kNormOff + 16 * lane) = ld_nc_128(src);
   }
   tc_fence_before();
   __syncthreads();
@@ -357,7 +367,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int grp = tn * 2 + half;  // 128-column head group of this warp
         const int kind = grp < a.q_groups ? ((grp & 1) ? 0 : 1) : (grp < a.q_groups + a.k_groups ? 2 : 0);
         qkv_group_epilogue<T>(a, tacc + (uint32_t)half * 128u, a.out + 2 * ((int64_t)m * a.ldo + grp * 128),
-                              m < a.M, kind, m < a.M ? m : 0);
+                              m < a.M, kind, m < a.M ? m : 0, smem + kNormOff);
       }
       tc_fence_before();
       __syncwarp();
