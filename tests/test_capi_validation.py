@@ -123,3 +123,14 @@ def test_python_wrappers_refuse_cpu_tensors():
         glue.gemv(x, torch.zeros(512, 1024, dtype=torch.bfloat16))
     with pytest.raises(ValueError):
         glue.swiglu(torch.zeros(2, 2048, dtype=torch.bfloat16), 1024)
+    with pytest.raises(ValueError):
+        glue.gemm_swiglu(x, torch.zeros(256, 1024, dtype=torch.bfloat16), 128)
+    with pytest.raises(ValueError):
+        glue.gemm_qkv_norm_rope(x.view(1, 2, 1024), torch.zeros(2560, 1024, dtype=torch.bfloat16), 8, 2,
+                                torch.zeros(128, dtype=torch.bfloat16), torch.zeros(128, dtype=torch.bfloat16),
+                                torch.zeros(1, 2, 32, dtype=torch.bfloat16), torch.zeros(1, 2, 32, dtype=torch.bfloat16),
+                                1e-6)
+    from butterfly_b200 import attention as A
+    q = torch.zeros(1, 8, 128, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        A.butterfly_compressed_attention(q, q[:, :2], q[:, :2], layout=None, local_window_tokens=64)
