@@ -326,6 +326,15 @@ __global__ void __launch_bounds__(decode_threads(G)) decode_kernel(const ActiveA
                            &pre_bar);
     }
   }
+  // V rows nk .. end of the last 16-key tile are zeroed (so that P = 0 there never meets
+  // stale bits); with the key count known before the wait (host-routed step) that happens
+  // here, off the critical path
+  const bool zero_early = pre && a.host_ns >= 0;
+  if (zero_early) {
+    const int nk0 = nraw + a.host_ns;
+    for (int c = threadIdx.x; c < ((nk0 + 15) / 16 * 16 - nk0) * 16; c += NT)
+      *reinterpret_cast<uint4*>(kv + (maxk + nk0 + (c >> 4)) * kDecPitch + (c & 15) * 16) = make_uint4(0, 0, 0, 0);
+  }
   // Launched with programmatic stream serialization: wait for the previous kernel of the
   // stream (and its memory) before touching anything it may write, then let the next
   // kernel start launching.
@@ -430,10 +439,11 @@ __global__ void __launch_bounds__(decode_threads(G)) decode_kernel(const ActiveA
   // (16-bit, in registers, already in the A-operand layout), and O += P V over the 128 value
   // columns (16 n-tiles, V fragments by ldmatrix.trans).  Rows >= G and keys >= nk are masked.
   const int gid = lane >> 2, tig = lane & 3;
-  // rows nk .. end of the last tile: zero V so that P = 0 there never meets stale bits
-  for (int c = threadIdx.x; c < ((nk + 15) / 16 * 16 - nk) * 16; c += NT)
-    *reinterpret_cast<uint4*>(kv + (maxk + nk + (c >> 4)) * kDecPitch + (c & 15) * 16) = make_uint4(0, 0, 0, 0);
-  __syncthreads();
+  if (!zero_early) {  // rows nk .. end of the last tile (see above)
+    for (int c = threadIdx.x; c < ((nk + 15) / 16 * 16 - nk) * 16; c += NT)
+      *reinterpret_cast<uint4*>(kv + (maxk + nk + (c >> 4)) * kDecPitch + (c & 15) * 16) = make_uint4(0, 0, 0, 0);
+    __syncthreads();
+  }
   uint32_t qa[8][4];  // Q fragments for the 8 k-steps of 16 head dims (rows gid, gid + 8)
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk) {
