@@ -170,6 +170,18 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
     return x2
 
 
+def _fused_lm_head_forward(self, x: torch.Tensor):
+    """The output projection for up to 8 rows (decode, or the kept position of a prefill)
+    as a weight-streaming GEMV (it streams the whole [vocab, hidden] matrix once)."""
+    K = int(x.shape[-1])
+    rows = x.numel() // K if K else 0
+    w = self.weight
+    if (x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and self.bias is None and 0 < rows <= 8
+            and K % 256 == 0 and K <= 8192 and w.dtype == x.dtype and w.is_contiguous()):
+        return glue.gemv(x.reshape(rows, K), w).view(*x.shape[:-1], int(w.shape[0]))
+    return type(self).forward(self, x)
+
+
 def _fused_norm_forward(self, x: torch.Tensor):
     if x.dtype not in (torch.bfloat16, torch.float16) or not x.is_cuda:
         return type(self).forward(self, x)
@@ -177,7 +189,8 @@ def _fused_norm_forward(self, x: torch.Tensor):
 
 
 def fuse_qwen_decoder_layers(model: nn.Module) -> list[int]:
-    """Run every swapped decoder layer (and the final norm) through the fused glue kernels.
+    """Run every swapped decoder layer (and the final norm, and the output projection for up
+    to 8 rows) through the fused glue kernels.
     Call after ``swap_qwen_attention_with_butterfly_cuda``; returns the fused layer indices."""
     decoder = _get_decoder_with_layers(model)
     fused = []
@@ -198,6 +211,9 @@ def fuse_qwen_decoder_layers(model: nn.Module) -> list[int]:
     norm = getattr(decoder, "norm", None)
     if fused and norm is not None and _is_qwen35_norm(norm) and "forward" not in norm.__dict__:
         norm.forward = types.MethodType(_fused_norm_forward, norm)
+    head = getattr(model, "lm_head", None)
+    if fused and isinstance(head, nn.Linear) and "forward" not in head.__dict__:
+        head.forward = types.MethodType(_fused_lm_head_forward, head)
     return fused
 
 
@@ -213,6 +229,9 @@ def unfuse_qwen_decoder_layers(model: nn.Module) -> list[int]:
     norm = getattr(decoder, "norm", None)
     if norm is not None:
         norm.__dict__.pop("forward", None)
+    head = getattr(model, "lm_head", None)
+    if isinstance(head, nn.Module):
+        head.__dict__.pop("forward", None)
     return out
 
 
