@@ -121,6 +121,8 @@ __device__ __forceinline__ uint4 ld_nc_128(const void* p) {
 // IEEE division sequence); callers round the result to 16 bits, where its few-ulp fp32
 // error is invisible except at rounding ties.  Saturates to 0 below x ~ -87.
 __device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+// silu(x) = x / (1 + e^-x) with the same two MUFU operations (callers round to 16 bits).
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
 // Pull the 128-byte line holding p into L2 (no registers held while it is in flight).
 __device__ __forceinline__ void prefetch_l2(const void* p) {

@@ -40,6 +40,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <string>
@@ -54,7 +55,11 @@ int* device_error_word();  // kernels.cu
 
 namespace {
 
-constexpr int kGemmThreads = 320;
+// Epilogue warps: 16 for SwiGLU (32 output columns of a row each: enough warps per SM
+// sub-partition to hide the MUFU and TMEM latencies), 8 for q/k/v (one 128-column head
+// group each; the norm + RoPE epilogue needs 119+ registers, which 576 threads cannot hold).
+__host__ __device__ constexpr int epi_warps(int epi) { return epi == 0 ? 16 : 8; }
+__host__ __device__ constexpr int gemm_threads(int epi) { return 64 + 32 * epi_warps(epi); }
 constexpr int kStages = 4;
 constexpr uint32_t kStageBytes = 3 * 16384;  // h tile, gate tile, up tile
 constexpr uint32_t kBarOff = kStages * kStageBytes;
@@ -214,8 +219,49 @@ __device__ __forceinline__ void qkv_group_epilogue(const GemmArgs& a, uint32_t t
   }
 }
 
+// Epilogue of one accumulator tile for this thread's row m: `half` selects the columns this
+// warp handles (SwiGLU: one of four 32-column parts of the 128 outputs; q/k/v: one of two
+// 128-column head groups), tn the tile's 256-column block.
 template <typename T, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__device__ __forceinline__ void tile_epilogue(const GemmArgs& a, uint32_t tacc, int m, int tn, int half,
+                                              const uint8_t* norm_smem) {
+  using namespace sm100;
+  if constexpr (EPI == kEpiSwiglu) {
+    // warp part `half` (0..3) of the row: output columns [32 half, 32 half + 32)
+    uint8_t* orow = a.out + 2 * ((int64_t)m * a.ldo + tn * 128);
+#pragma unroll 1
+    for (int c = half * 32; c < half * 32 + 32; c += 16) {
+      float g[16], u[16];
+      tmem_ld16(tacc + (uint32_t)c, g);
+      tmem_ld16(tacc + 128u + (uint32_t)c, u);
+      tmem_ld_wait();
+      uint32_t w[8];
+#pragma unroll
+      for (int e = 0; e < 16; e += 2) {
+        // gate products rounded (as a pair), silu rounded, times the rounded up products
+        const float2 gr = ElemTraits<T>::unpack2(ElemTraits<T>::pack2(g[e], g[e + 1]));
+        w[e >> 1] = ElemTraits<T>::mul2(ElemTraits<T>::pack2(silu_fast(gr.x), silu_fast(gr.y)),
+                                        ElemTraits<T>::pack2(u[e], u[e + 1]));
+      }
+      if (m < a.M) {
+        if (a.st256) {
+          st_256(orow + 2 * c, w);
+        } else {
+          st_128(orow + 2 * c, make_uint4(w[0], w[1], w[2], w[3]));
+          st_128(orow + 2 * c + 16, make_uint4(w[4], w[5], w[6], w[7]));
+        }
+      }
+    }
+  } else {
+    const int grp = tn * 2 + half;  // 128-column head group of this warp
+    const int kind = grp < a.q_groups ? ((grp & 1) ? 0 : 1) : (grp < a.q_groups + a.k_groups ? 2 : 0);
+    qkv_group_epilogue<T>(a, tacc + (uint32_t)half * 128u, a.out + 2 * ((int64_t)m * a.ldo + grp * 128), m < a.M,
+                          kind, m < a.M ? m : 0, norm_smem);
+  }
+}
+
+template <typename T, int EPI>
+__global__ void __launch_bounds__(gemm_threads(EPI), 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                       const __grid_constant__ GemmArgs a) {
   using namespace sm100;
@@ -240,7 +286,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accfull[b], 1);
-      mbar_init(&accempty[b], 8);
+      mbar_init(&accempty[b], epi_warps(EPI));
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -328,7 +374,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ epilogue
-    const int q = warp & 3, half = (warp - 2) >> 2;
+    const int q = warp & 3, half = (warp - 2) >> 2;  // TMEM lane quarter; column part
     const int row = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     int tc = 0;
@@ -337,38 +383,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait(&accfull[buf], (uint32_t)(tc >> 1) & 1u, abort_flag, 25, a.err)) break;
       tc_fence_after();
       const int m = (tile / a.tiles_n) * 128 + row, tn = tile % a.tiles_n;
-      const uint32_t tacc = tmem + lane_off + (uint32_t)buf * 256u;
-      if constexpr (EPI == kEpiSwiglu) {
-        uint8_t* orow = a.out + 2 * ((int64_t)m * a.ldo + tn * 128);
-#pragma unroll 1
-        for (int c = half * 64; c < half * 64 + 64; c += 16) {
-          float g[16], u[16];
-          tmem_ld16(tacc + (uint32_t)c, g);
-          tmem_ld16(tacc + 128u + (uint32_t)c, u);
-          tmem_ld_wait();
-          uint32_t w[8];
-#pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            const float g0 = round_to<T>(g[e]), g1 = round_to<T>(g[e + 1]);
-            const float s0 = round_to<T>(g0 / (1.f + __expf(-g0))), s1 = round_to<T>(g1 / (1.f + __expf(-g1)));
-            w[e >> 1] = ElemTraits<T>::mul2(ElemTraits<T>::pack2(s0, s1),
-                                            ElemTraits<T>::pack2(u[e], u[e + 1]));
-          }
-          if (m < a.M) {
-            if (a.st256) {
-              st_256(orow + 2 * c, w);
-            } else {
-              st_128(orow + 2 * c, make_uint4(w[0], w[1], w[2], w[3]));
-              st_128(orow + 2 * c + 16, make_uint4(w[4], w[5], w[6], w[7]));
-            }
-          }
-        }
-      } else {
-        const int grp = tn * 2 + half;  // 128-column head group of this warp
-        const int kind = grp < a.q_groups ? ((grp & 1) ? 0 : 1) : (grp < a.q_groups + a.k_groups ? 2 : 0);
-        qkv_group_epilogue<T>(a, tacc + (uint32_t)half * 128u, a.out + 2 * ((int64_t)m * a.ldo + grp * 128),
-                              m < a.M, kind, m < a.M ? m : 0, smem + kNormOff);
-      }
+      tile_epilogue<T, EPI>(a, tmem + lane_off + (uint32_t)buf * 256u, m, tn, half, smem + kNormOff);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&accempty[buf]);
@@ -379,6 +394,172 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------- CTA-pair form
+// The same GEMM on CTA pairs (clusters of 2, tcgen05 cta_group::2): a pair computes a
+// 256-row x 256-column tile as one M = 256, N = 256 MMA per 16-wide k-step.  CTA r holds
+// h rows m0 + 128 r and the r-th 128-row W box (gate / up rows for SwiGLU), so per k-block a
+// CTA stages 32 KB instead of 48 KB: each W byte is read from shared memory once per 256
+// output rows instead of once per 128.  Both CTAs' tiles land on the leader's (rank 0)
+// `full` barrier; the leader's MMA warp issues for the pair and its commits arrive on the
+// `empty` / `accfull` barriers of both CTAs; both CTAs' epilogue warps arrive on the
+// leader's `accempty`.  Each CTA's epilogue reads its own 128 accumulator rows (all 256
+// columns), exactly as in the single-CTA form.
+constexpr int kPairStages = 6;
+constexpr uint32_t kPairStageBytes = 2 * 16384;  // h tile, one W box
+constexpr uint32_t kPairBarOff = kPairStages * kPairStageBytes;
+constexpr uint32_t kPairNormOff = kPairBarOff + 256;
+constexpr uint32_t kPairSmem = kPairNormOff + 512 + 1024;
+
+template <typename T, int EPI>
+__global__ void __launch_bounds__(gemm_threads(EPI), 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                     const __grid_constant__ GemmArgs a) {
+  using namespace sm100;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  extern __shared__ uint8_t gsm_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPairBarOff);
+  uint64_t* full = bars;                       // [kPairStages] both CTAs' tiles landed (leader's copy used)
+  uint64_t* empty = bars + kPairStages;        // [kPairStages] stage consumed (both CTAs)
+  uint64_t* accfull = bars + 2 * kPairStages;  // [2] accumulator buffer complete (both CTAs)
+  uint64_t* accempty = accfull + 2;            // [2] buffer read out by 16 epilogue warps (leader's copy)
+  uint64_t* drain = accempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accfull[b], 1);
+      mbar_init(&accempty[b], 2 * epi_warps(EPI));
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmW);
+  }
+  if (EPI == kEpiQKNorm && warp == 2) {
+    const uint8_t* src = lane < 16 ? a.qn_w + 16 * lane : a.kn_w + 16 * (lane - 16);
+    *reinterpret_cast<uint4*>(smem + kPairNormOff + 16 * lane) = ld_nc_128(src);
+  }
+  tc_fence_before();
+  // both CTAs' barriers are initialised before either CTA signals the other's
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int KB = a.K >> 6;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producers (both CTAs)
+    if (lane == 0) {
+      const uint32_t full0 = mapa_shared(smem_u32(full), 0);  // leader's full[0]
+      int it = 0;
+      for (int tile = pair; tile < a.total_tiles && !*abort_flag; tile += npairs) {
+        const int m0 = (tile / a.tiles_n) * 256 + (int)rank * 128;
+        const int w0 = (rank ? a.b2 : 0) + (tile % a.tiles_n) * a.tile_w;
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % kPairStages, use = it / kPairStages;
+          if (use > 0 && !mbar_wait(&empty[s], (uint32_t)(use - 1) & 1u, abort_flag, 30, a.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + (uint32_t)s * kPairStageBytes;
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * kPairStageBytes);
+          const uint32_t fb = full0 + (uint32_t)s * 8u;
+          tma_load_4d_pair(st, &tmA, fb, kb * 64, m0, 0, 0);
+          tma_load_4d_pair(st + 16384, &tmW, fb, kb * 64, w0, 0, 0);
+        }
+        if (!ok) break;
+      }
+      // the leader drains the last loads of each stage (its barrier counts both CTAs' bytes)
+      if (leader) {
+        volatile int never_abort = 0;
+        for (int d = it - 1; d >= 0 && d >= it - kPairStages; --d)
+          mbar_wait(&full[d % kPairStages], (uint32_t)(d / kPairStages) & 1u, &never_abort, 31, a.err);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (leader only)
+    if (leader) {
+      constexpr uint32_t fmt = ElemTraits<T>::kUmmaFormat;
+      const uint32_t idesc = idesc_f16(256, 256, fmt, false);
+      auto wait_all = [&](uint64_t* bar, uint32_t parity, int site) -> bool {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, site, a.err)) != 0;
+      };
+      int it = 0, tc = 0;
+      bool ok = true;
+      for (int tile = pair; tile < a.total_tiles && ok; tile += npairs, ++tc) {
+        const int buf = tc & 1, use = tc >> 1;
+        if (use > 0 && !wait_all(&accempty[buf], (uint32_t)(use - 1) & 1u, 32)) break;
+        tc_fence_after();
+        const uint32_t dacc = tmem + (uint32_t)buf * 256u;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % kPairStages;
+          if (!wait_all(&full[s], (uint32_t)(it / kPairStages) & 1u, 33)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + (uint32_t)s * kPairStageBytes);
+          const uint64_t da = desc_sw128(st, 16, 1024), db = desc_sw128(st + 16384, 16, 1024);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f16_ss_pair_warp(dacc, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (kb | kk) != 0);
+          mma_commit_pair_both_warp(&empty[s]);
+        }
+        if (ok) mma_commit_pair_both_warp(&accfull[buf]);
+      }
+      volatile int never_abort = 0;
+      mma_commit_pair_local_warp(drain);
+      if (lane == 0) mbar_wait(drain, 0, &never_abort, 34, a.err);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3, half = (warp - 2) >> 2;  // TMEM lane quarter; column part
+    const int row = q * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const uint32_t accempty0 = mapa_shared(smem_u32(accempty), 0);
+    int tc = 0;
+    for (int tile = pair; tile < a.total_tiles; tile += npairs, ++tc) {
+      const int buf = tc & 1;
+      if (!mbar_wait(&accfull[buf], (uint32_t)(tc >> 1) & 1u, abort_flag, 35, a.err)) break;
+      tc_fence_after();
+      const int m = (tile / a.tiles_n) * 256 + (int)rank * 128 + row, tn = tile % a.tiles_n;
+      tile_epilogue<T, EPI>(a, tmem + lane_off + (uint32_t)buf * 256u, m, tn, half, smem + kPairNormOff);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(accempty0 + (uint32_t)buf * 8u);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  // neither CTA leaves (or frees its TMEM) while the pair's MMAs, commits or remote arrivals
+  // may still reach it
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
@@ -433,12 +614,31 @@ using namespace bna;
 namespace bna {
 namespace {
 
+// CTA-pair tiles unless BNA_GEMM_CTA_PAIR=0 (the single-CTA form, kept for comparison).
+bool use_cta_pairs() {
+  static const bool on = [] {
+    const char* e = std::getenv("BNA_GEMM_CTA_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 int launch_gemm(int epi, const CUtensorMap& ma, const CUtensorMap& mw, GemmArgs& a, int dtype, void* stream) {
   a.err = device_error_word();
   int dev = 0;
   cudaGetDevice(&dev);
   const int nsm = sm_count(dev);
-  const int grid = a.total_tiles < nsm ? a.total_tiles : nsm;
+  const bool pair = use_cta_pairs() && nsm >= 2;
+  int grid;
+  if (pair) {
+    // a pair tile covers 256 rows; two CTAs per tile, an even grid of at most nsm CTAs
+    a.total_tiles = (int)(((int64_t)a.M + 255) / 256) * a.tiles_n;
+    grid = 2 * (a.total_tiles < nsm / 2 ? a.total_tiles : nsm / 2);
+  } else {
+    a.total_tiles = (int)(((int64_t)a.M + 127) / 128) * a.tiles_n;
+    grid = a.total_tiles < nsm ? a.total_tiles : nsm;
+  }
+  const int smem_bytes = pair ? (int)kPairSmem : (int)kGemmSmem;
   auto launch = [&](auto kern) {
     static std::mutex mu;
     static std::map<std::pair<const void*, int>, bool> done;
@@ -446,26 +646,36 @@ int launch_gemm(int epi, const CUtensorMap& ma, const CUtensorMap& mw, GemmArgs&
       std::lock_guard<std::mutex> g(mu);
       bool& d = done[{reinterpret_cast<const void*>(kern), dev}];
       if (!d) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem);
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+        if (pair) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
         d = true;
       }
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kGemmThreads);
-    cfg.dynamicSmemBytes = kGemmSmem;
+    cfg.blockDim = dim3(gemm_threads(epi));
+    cfg.dynamicSmemBytes = smem_bytes;
     cfg.stream = static_cast<cudaStream_t>(stream);
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[0].val.programmaticStreamSerializationAllowed = 1;
+    at[1].id = cudaLaunchAttributeClusterDimension;
+    at[1].val.clusterDim.x = 2;
+    at[1].val.clusterDim.y = 1;
+    at[1].val.clusterDim.z = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pair ? 2 : 1;
     cudaLaunchKernelEx(&cfg, kern, ma, mw, a);
   };
   const bool bf = dtype == BNA_BF16;
-  if (epi == kEpiSwiglu) bf ? launch(gemm_sm100_kernel<__nv_bfloat16, kEpiSwiglu>) : launch(gemm_sm100_kernel<__half, kEpiSwiglu>);
-  else bf ? launch(gemm_sm100_kernel<__nv_bfloat16, kEpiQKNorm>) : launch(gemm_sm100_kernel<__half, kEpiQKNorm>);
-  return check_cuda(cudaGetLastError(), "gemm_sm100 launch");
+  if (pair) {
+    if (epi == kEpiSwiglu) bf ? launch(gemm_pair_kernel<__nv_bfloat16, kEpiSwiglu>) : launch(gemm_pair_kernel<__half, kEpiSwiglu>);
+    else bf ? launch(gemm_pair_kernel<__nv_bfloat16, kEpiQKNorm>) : launch(gemm_pair_kernel<__half, kEpiQKNorm>);
+  } else {
+    if (epi == kEpiSwiglu) bf ? launch(gemm_sm100_kernel<__nv_bfloat16, kEpiSwiglu>) : launch(gemm_sm100_kernel<__half, kEpiSwiglu>);
+    else bf ? launch(gemm_sm100_kernel<__nv_bfloat16, kEpiQKNorm>) : launch(gemm_sm100_kernel<__half, kEpiQKNorm>);
+  }
+  return check_cuda(cudaGetLastError(), pair ? "gemm_sm100 (CTA pairs) launch" : "gemm_sm100 launch");
 }
 
 int check_gemm_common(const void* h, int64_t ldh, const void* w, int64_t ldw, const void* out, int64_t ldo, int64_t M,

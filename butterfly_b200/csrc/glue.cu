@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const SwigluArgs a) {
   unpack8(ld_nc_128(base + 2 * a.up_off), u, bf);
   float y[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) y[e] = round_to<T>(g[e] / (1.f + __expf(-g[e]))) * u[e];
+  for (int e = 0; e < 8; ++e) y[e] = round_to<T>(silu_fast(g[e])) * u[e];
   st_128(a.out + 16 * (int64_t)i, pack8<T>(y));
 }
 
