@@ -59,7 +59,8 @@ def test_gemm_swiglu_rejects_bad_shapes():
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("B,T,K,Hq,Hkv,rot", [(1, 1000, 1024, 8, 2, 32), (2, 300, 2560, 16, 4, 64), (1, 70, 1024, 8, 2, 128)])
+@pytest.mark.parametrize("B,T,K,Hq,Hkv,rot", [(1, 1000, 1024, 8, 2, 32), (2, 300, 2560, 16, 4, 64), (1, 70, 1024, 8, 2, 128),
+                                                 (1, 8192, 1024, 8, 2, 32)])
 def test_gemm_qkv_norm_rope_matches_unfused(dtype, B, T, K, Hq, Hkv, rot):
     """The q/k/v GEMM with the q/k norm + RoPE epilogue against cuBLAS + bna_qk_norm_rope."""
     g = torch.Generator(device="cuda").manual_seed(T + K)
