@@ -55,10 +55,10 @@ int* device_error_word();  // kernels.cu
 
 namespace {
 
-// Epilogue warps: 16 for SwiGLU (32 output columns of a row each: enough warps per SM
-// sub-partition to hide the MUFU and TMEM latencies), 8 for q/k/v (one 128-column head
+// Epilogue warps: 16 for SwiGLU and the residual add (a quarter of a row's outputs each:
+// enough warps per SM sub-partition to hide the MUFU, TMEM and load latencies), 8 for q/k/v (one 128-column head
 // group each; the norm + RoPE epilogue needs 119+ registers, which 576 threads cannot hold).
-__host__ __device__ constexpr int epi_warps(int epi) { return epi == 0 ? 16 : 8; }
+__host__ __device__ constexpr int epi_warps(int epi) { return epi == 1 ? 8 : 16; }
 __host__ __device__ constexpr int gemm_threads(int epi) { return 64 + 32 * epi_warps(epi); }
 constexpr int kStages = 4;
 constexpr uint32_t kStageBytes = 3 * 16384;  // h tile, gate tile, up tile
@@ -66,7 +66,7 @@ constexpr uint32_t kBarOff = kStages * kStageBytes;
 constexpr uint32_t kNormOff = kBarOff + 256;          // q / k norm weights (2 x 128 16-bit values)
 constexpr uint32_t kGemmSmem = kNormOff + 512 + 1024;  // + 1024-byte alignment slack
 
-enum { kEpiSwiglu = 0, kEpiQKNorm = 1 };
+enum { kEpiSwiglu = 0, kEpiQKNorm = 1, kEpiResid = 2 };
 
 struct GemmArgs {
   int M, K;
@@ -86,6 +86,9 @@ struct GemmArgs {
   const uint8_t* sn;
   int rot;
   float eps;
+  // residual epilogue: out = round(acc + res), res [M, N] of row stride ldr (may be out)
+  const uint8_t* res;
+  int64_t ldr;
 };
 
 __device__ __forceinline__ void unpack8v(const uint4& u, float* f, bool bf) {
@@ -224,7 +227,7 @@ __device__ __forceinline__ void qkv_group_epilogue(const GemmArgs& a, uint32_t t
 // 128-column head groups), tn the tile's 256-column block.
 template <typename T, int EPI>
 __device__ __forceinline__ void tile_epilogue(const GemmArgs& a, uint32_t tacc, int m, int tn, int half,
-                                              const uint8_t* norm_smem) {
+                                              const uint8_t* norm_smem, const uint4* rv) {
   using namespace sm100;
   if constexpr (EPI == kEpiSwiglu) {
     // warp part `half` (0..3) of the row: output columns [32 half, 32 half + 32)
@@ -252,11 +255,53 @@ __device__ __forceinline__ void tile_epilogue(const GemmArgs& a, uint32_t tacc, 
         }
       }
     }
+  } else if constexpr (EPI == kEpiResid) {
+    // warp part `half` (0..3) of the row: columns [64 half, 64 half + 64) of the tile; rv
+    // holds the residual of those columns, loaded before the accumulator wait by the thread
+    // that writes the sums (so in place is allowed)
+    uint8_t* orow = a.out + 2 * ((int64_t)m * a.ldo + (int64_t)tn * 256 + half * 64);
+#pragma unroll
+    for (int c = 0; c < 64; c += 16) {
+      float x[16];
+      tmem_ld16(tacc + (uint32_t)(half * 64 + c), x);
+      tmem_ld_wait();
+      const uint4 r0 = rv[c >> 3], r1 = rv[(c >> 3) + 1];
+      const uint32_t rw[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+      uint32_t w[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        // as the eager ops: the projection rounded, then the residual added and rounded
+        const float2 p2 = ElemTraits<T>::unpack2(ElemTraits<T>::pack2(x[2 * e], x[2 * e + 1]));
+        const float2 r2 = ElemTraits<T>::unpack2(rw[e]);
+        w[e] = ElemTraits<T>::pack2(p2.x + r2.x, p2.y + r2.y);
+      }
+      if (m < a.M) {
+        if (a.st256) {
+          st_256(orow + 2 * c, w);
+        } else {
+          st_128(orow + 2 * c, make_uint4(w[0], w[1], w[2], w[3]));
+          st_128(orow + 2 * c + 16, make_uint4(w[4], w[5], w[6], w[7]));
+        }
+      }
+    }
   } else {
     const int grp = tn * 2 + half;  // 128-column head group of this warp
     const int kind = grp < a.q_groups ? ((grp & 1) ? 0 : 1) : (grp < a.q_groups + a.k_groups ? 2 : 0);
     qkv_group_epilogue<T>(a, tacc + (uint32_t)half * 128u, a.out + 2 * ((int64_t)m * a.ldo + grp * 128), m < a.M,
                           kind, m < a.M ? m : 0, norm_smem);
+  }
+}
+
+// Residual epilogue: this thread's 64 residual values of tile `tile` (row m), loaded before
+// the accumulator wait so their latency overlaps it.
+__device__ __forceinline__ void load_residual(const GemmArgs& a, int m, int tn, int half, uint4* rv) {
+  if (m < a.M) {
+    const uint8_t* rrow = a.res + 2 * ((int64_t)m * a.ldr + (int64_t)tn * 256 + half * 64);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) rv[i] = ld_128(rrow + 16 * i);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) rv[i] = make_uint4(0, 0, 0, 0);
   }
 }
 
@@ -380,10 +425,12 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
     int tc = 0;
     for (int tile = blockIdx.x; tile < a.total_tiles; tile += gridDim.x, ++tc) {
       const int buf = tc & 1;
+      const int m = (tile / a.tiles_n) * 128 + row, tn = tile % a.tiles_n;
+      uint4 rv[EPI == kEpiResid ? 8 : 1];
+      if constexpr (EPI == kEpiResid) load_residual(a, m, tn, half, rv);
       if (!mbar_wait(&accfull[buf], (uint32_t)(tc >> 1) & 1u, abort_flag, 25, a.err)) break;
       tc_fence_after();
-      const int m = (tile / a.tiles_n) * 128 + row, tn = tile % a.tiles_n;
-      tile_epilogue<T, EPI>(a, tmem + lane_off + (uint32_t)buf * 256u, m, tn, half, smem + kNormOff);
+      tile_epilogue<T, EPI>(a, tmem + lane_off + (uint32_t)buf * 256u, m, tn, half, smem + kNormOff, rv);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&accempty[buf]);
@@ -543,10 +590,12 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
     int tc = 0;
     for (int tile = pair; tile < a.total_tiles; tile += npairs, ++tc) {
       const int buf = tc & 1;
+      const int m = (tile / a.tiles_n) * 256 + (int)rank * 128 + row, tn = tile % a.tiles_n;
+      uint4 rv[EPI == kEpiResid ? 8 : 1];
+      if constexpr (EPI == kEpiResid) load_residual(a, m, tn, half, rv);
       if (!mbar_wait(&accfull[buf], (uint32_t)(tc >> 1) & 1u, abort_flag, 35, a.err)) break;
       tc_fence_after();
-      const int m = (tile / a.tiles_n) * 256 + (int)rank * 128 + row, tn = tile % a.tiles_n;
-      tile_epilogue<T, EPI>(a, tmem + lane_off + (uint32_t)buf * 256u, m, tn, half, smem + kPairNormOff);
+      tile_epilogue<T, EPI>(a, tmem + lane_off + (uint32_t)buf * 256u, m, tn, half, smem + kPairNormOff, rv);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(accempty0 + (uint32_t)buf * 8u);
@@ -670,10 +719,12 @@ int launch_gemm(int epi, const CUtensorMap& ma, const CUtensorMap& mw, GemmArgs&
   const bool bf = dtype == BNA_BF16;
   if (pair) {
     if (epi == kEpiSwiglu) bf ? launch(gemm_pair_kernel<__nv_bfloat16, kEpiSwiglu>) : launch(gemm_pair_kernel<__half, kEpiSwiglu>);
-    else bf ? launch(gemm_pair_kernel<__nv_bfloat16, kEpiQKNorm>) : launch(gemm_pair_kernel<__half, kEpiQKNorm>);
+    else if (epi == kEpiQKNorm) bf ? launch(gemm_pair_kernel<__nv_bfloat16, kEpiQKNorm>) : launch(gemm_pair_kernel<__half, kEpiQKNorm>);
+    else bf ? launch(gemm_pair_kernel<__nv_bfloat16, kEpiResid>) : launch(gemm_pair_kernel<__half, kEpiResid>);
   } else {
     if (epi == kEpiSwiglu) bf ? launch(gemm_sm100_kernel<__nv_bfloat16, kEpiSwiglu>) : launch(gemm_sm100_kernel<__half, kEpiSwiglu>);
-    else bf ? launch(gemm_sm100_kernel<__nv_bfloat16, kEpiQKNorm>) : launch(gemm_sm100_kernel<__half, kEpiQKNorm>);
+    else if (epi == kEpiQKNorm) bf ? launch(gemm_sm100_kernel<__nv_bfloat16, kEpiQKNorm>) : launch(gemm_sm100_kernel<__half, kEpiQKNorm>);
+    else bf ? launch(gemm_sm100_kernel<__nv_bfloat16, kEpiResid>) : launch(gemm_sm100_kernel<__half, kEpiResid>);
   }
   return check_cuda(cudaGetLastError(), pair ? "gemm_sm100 (CTA pairs) launch" : "gemm_sm100 launch");
 }
@@ -759,4 +810,37 @@ extern "C" BNA_API int bna_gemm_qkv_norm_rope(const void* h, int64_t ldh, const 
   a.eps = eps;
   a.st256 = ((reinterpret_cast<uintptr_t>(out) & 31) == 0 && (ldo * 2) % 32 == 0) ? 1 : 0;
   return launch_gemm(kEpiQKNorm, ma, mw, a, dtype, stream);
+}
+
+extern "C" BNA_API int bna_gemm_residual(const void* h, int64_t ldh, const void* w, int64_t ldw, const void* res,
+                                         int64_t ldr, void* out, int64_t ldo, int64_t M, int32_t K, int32_t N,
+                                         int32_t dtype, void* stream) {
+  if (int rc = check_gemm_common(h, ldh, w, ldw, out, ldo, M, K, dtype, "gemm_residual")) return rc;
+  if (N <= 0 || N % 256) return fail(BNA_UNSUPPORTED, "gemm_residual: N must be a positive multiple of 256");
+  if (ldo < N || ldr < N) return fail(BNA_BAD_STRIDE, "gemm_residual: output / residual row stride below N");
+  if (M > 0 && !res) return fail(BNA_BAD_SHAPE, "gemm_residual: null residual");
+  if (ldr % 8 || (reinterpret_cast<uintptr_t>(res) & 15)) return fail(BNA_BAD_STRIDE, "gemm_residual: residual must be 16-byte aligned with a row stride of 8 elements");
+  if (res != out || ldr != ldo) {
+    // the residual is read by the thread that writes the same element; any other overlap races
+    const uintptr_t r0 = reinterpret_cast<uintptr_t>(res), o0 = reinterpret_cast<uintptr_t>(out);
+    const uintptr_t r1 = r0 + 2 * (uintptr_t)((M - 1) * ldr + N), o1 = o0 + 2 * (uintptr_t)((M - 1) * ldo + N);
+    if (M > 0 && r0 < o1 && o0 < r1) return fail(BNA_BAD_SHAPE, "gemm_residual: residual overlaps the output other than in place");
+  }
+  if (M == 0) return BNA_OK;
+  const CUtensorMapDataType dt = dtype == BNA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ma, mw;
+  if (int rc = encode_rows(&ma, h, M, K, ldh, dt, "h")) return rc;
+  if (int rc = encode_rows(&mw, w, N, K, ldw, dt, "w")) return rc;
+  GemmArgs a{};
+  a.M = (int)M;
+  a.K = K;
+  a.tiles_n = N / 256;
+  a.b2 = 128;
+  a.tile_w = 256;
+  a.out = static_cast<uint8_t*>(out);
+  a.ldo = ldo;
+  a.res = static_cast<const uint8_t*>(res);
+  a.ldr = ldr;
+  a.st256 = ((reinterpret_cast<uintptr_t>(out) & 31) == 0 && (ldo * 2) % 32 == 0) ? 1 : 0;
+  return launch_gemm(kEpiResid, ma, mw, a, dtype, stream);
 }

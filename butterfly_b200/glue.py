@@ -193,6 +193,32 @@ def gemm_qkv_norm_rope(h: torch.Tensor, w_qkv: torch.Tensor, num_q_heads: int, n
     return out
 
 
+def gemm_residual(h: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """residual + h @ w^T for h [..., K], w [N, K] row-major and residual [..., N] with the
+    eager ops' rounding (the projection rounded, then the sum), on the tcgen05 GEMM with the
+    residual add in its epilogue.
+    ``out`` may be ``residual`` itself (an in-place add, as ``residual.addmm_``)."""
+    _lib.require_cuda(h, w, residual)
+    K = int(h.shape[-1])
+    N = int(w.shape[0])
+    rows, ldh = _rows(h, K)
+    if w.dim() != 2 or int(w.shape[1]) != K or w.stride(1) != 1 or w.dtype != h.dtype:
+        raise ValueError("w must be a row-major [N, K] matrix of h's dtype")
+    if tuple(residual.shape) != (*h.shape[:-1], N) or residual.dtype != h.dtype:
+        raise ValueError(f"residual must be [..., {N}] with h's leading dims and dtype")
+    rr, ldr = _rows(residual, N)
+    if out is None:
+        out = torch.empty(residual.shape, device=h.device, dtype=h.dtype)
+    elif tuple(out.shape) != tuple(residual.shape) or out.dtype != h.dtype:
+        raise ValueError("out must match residual")
+    ro, ldo = _rows(out, N)
+    _lib.check(_lib.lib().bna_gemm_residual(h.data_ptr(), ldh, w.data_ptr(), w.stride(0), residual.data_ptr(), ldr,
+                                            out.data_ptr(), ldo, rows, K, N, _lib.dtype_code(h.dtype),
+                                            _lib.stream_ptr(h.device)))
+    return out
+
+
 def _mat(x: torch.Tensor, K: int) -> tuple[int, int]:
     """(tokens, row stride) of a [M, K] matrix view with a contiguous last dim."""
     if x.dim() != 2 or x.shape[1] != K or x.stride(1) != 1:

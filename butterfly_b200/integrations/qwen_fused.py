@@ -80,6 +80,10 @@ class _FusedState:
         # and the q/k/v GEMM with the q/k norm + RoPE epilogue: 128-wide heads, N by 256
         self.gemm_qkv = (src.q_proj.in_features % 64 == 0 and self.dh == 128 and
                          int(self.w_qkv.shape[0]) % 256 == 0)
+        # and o_proj / down_proj with the residual add in the epilogue: N (hidden) by 256
+        hidden = src.o_proj.out_features
+        self.gemm_resid = (hidden % 256 == 0 and src.o_proj.in_features % 64 == 0 and self.inter % 64 == 0
+                           and mlp.down_proj.out_features == hidden)
 
 
 def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=None, attention_mask=None,
@@ -158,14 +162,21 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
         y = glue.gate_sigmoid_mul(out.transpose(1, 2), qg[..., dh:])  # out storage is [B,T,hq,dh]
     else:
         y = gated
-    a = F.linear(y, src.o_proj.weight)
-    h2, x2 = glue.rmsnorm(a, self.post_attention_layernorm.weight, self.post_attention_layernorm.eps,
-                          residual=x, want_sum=True)
+    if st.gemm_resid:  # o_proj with the residual add in the epilogue, then the norm
+        x2 = glue.gemm_residual(y, src.o_proj.weight, x)
+        h2 = glue.rmsnorm(x2, self.post_attention_layernorm.weight, self.post_attention_layernorm.eps)
+    else:
+        a = F.linear(y, src.o_proj.weight)
+        h2, x2 = glue.rmsnorm(a, self.post_attention_layernorm.weight, self.post_attention_layernorm.eps,
+                              residual=x, want_sum=True)
     if st.gemm_swiglu:  # gate/up GEMM with SwiGLU in the epilogue (no [T, 2*inter] product in HBM)
         act = glue.gemm_swiglu(h2, st.w_gu, st.inter)
     else:
         act = glue.swiglu(F.linear(h2, st.w_gu), st.inter)
-    x2.view(-1, H).addmm_(act.view(-1, st.inter), self.mlp.down_proj.weight.t())
+    if st.gemm_resid:  # down_proj accumulated onto the residual in place
+        glue.gemm_residual(act, self.mlp.down_proj.weight, x2, out=x2)
+    else:
+        x2.view(-1, H).addmm_(act.view(-1, st.inter), self.mlp.down_proj.weight.t())
     attn._profile(T, k_len_after, backend, hit, t0, fused=True)
     return x2
 

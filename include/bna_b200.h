@@ -267,6 +267,16 @@ BNA_API int bna_gemm_qkv_norm_rope(const void* h, int64_t ldh, const void* w, in
                                    const void* q_norm_w, const void* k_norm_w, const void* cos, const void* sin,
                                    int32_t rot, float eps, int32_t dtype, void* stream);
 
+/* A projection followed by the decoder layer's residual add, on tcgen05 tensor cores:
+ * out[m, n] = round(round(h[m,:] . w[n,:]) + res[m, n]) for m < M, n < N: the projection
+ * rounded, then the residual added and rounded, as the eager ops of transformers'
+ * Qwen3_5DecoderLayer (residual + o_proj(attn), residual + down_proj(mlp); qwen_torch.py
+ * :1585-1591 feeds o_proj).  out may be res
+ * (same pointer and row stride: an in-place add); any other overlap is rejected.  K a
+ * multiple of 64, N of 256, row strides multiples of 8 elements, pointers 16-byte aligned. */
+BNA_API int bna_gemm_residual(const void* h, int64_t ldh, const void* w, int64_t ldw, const void* res, int64_t ldr,
+                              void* out, int64_t ldo, int64_t M, int32_t K, int32_t N, int32_t dtype, void* stream);
+
 /* Decode-time projections for 1..8 tokens (y = W x per token, W [out_features,
  * in_features] row-major, in_features a multiple of 256), with the layer step before the
  * projection fused in front of it and the one after it fused behind it.  Replace the

@@ -88,3 +88,47 @@ def test_gemm_qkv_norm_rope_matches_unfused(dtype, B, T, K, Hq, Hkv, rot):
         scale = float(b.abs().max())
         assert float((a - b).abs().max()) <= 0.03 * scale
         assert float((a == b).float().mean()) >= 0.85
+
+
+def _check_residual(h, w, res, got):
+    ref16 = res + F.linear(h, w).view(res.shape)  # the eager decoder layer's ops
+    ref32 = h.float() @ w.float().t() + res.float()
+    scale = float(ref32.abs().max())
+    assert float((got.float() - ref16.float()).abs().max()) <= 0.01 * scale
+    assert float((got == ref16).float().mean()) >= 0.90
+    e_got = float((got.float() - ref32).abs().max())
+    e_ref = float((ref16.float() - ref32).abs().max())
+    assert e_got <= e_ref + 0.005 * scale, (e_got, e_ref, scale)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,K,N", [(1000, 1024, 1024), (131, 3584, 1024), (1, 64, 256), (8192, 3584, 1024),
+                                   (700, 9728, 2560)])
+def test_gemm_residual_matches_cublas_addmm(dtype, M, K, N):
+    """o_proj / down_proj with the residual add in the epilogue (bna_gemm_residual) against
+    the eager ops it replaces (cuBLAS projection, then the rounded add), out of place and
+    in place."""
+    g = torch.Generator(device="cuda").manual_seed(M + K + N)
+    h = torch.randn(M, K, device="cuda", generator=g).to(dtype)
+    w = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).to(dtype)
+    res = torch.randn(M, N, device="cuda", generator=g).to(dtype)
+    got = glue.gemm_residual(h, w, res)
+    _check_residual(h, w, res, got)
+    inplace = res.clone()
+    out = glue.gemm_residual(h, w, inplace, out=inplace)
+    assert out.data_ptr() == inplace.data_ptr()
+    assert torch.equal(inplace, got)
+
+
+def test_gemm_residual_strided_and_rejects_partial_overlap():
+    g = torch.Generator(device="cuda").manual_seed(5)
+    big = torch.randn(2, 300, 1536, device="cuda", generator=g).bfloat16()
+    h = big[..., 256:1280]
+    w = (torch.randn(1024, 1024, device="cuda", generator=g) / 32).bfloat16()
+    res = torch.randn(2, 300, 1024, device="cuda", generator=g).bfloat16()
+    got = glue.gemm_residual(h, w, res)
+    assert got.shape == (2, 300, 1024)
+    _check_residual(h.reshape(600, 1024).contiguous(), w, res.reshape(600, 1024), got.reshape(600, 1024))
+    buf = torch.zeros(601, 1024, device="cuda").bfloat16()
+    with pytest.raises(ValueError):
+        glue.gemm_residual(torch.randn(600, 1024, device="cuda").bfloat16(), w, buf[:600], out=buf[1:])
