@@ -24,7 +24,7 @@ EXPORTED = (
     "bna_active_attention", "bna_cache_append", "bna_decode_step", "bna_prefill_attention_static_scratch",
     "bna_rmsnorm", "bna_qk_norm_rope", "bna_gate_sigmoid_mul", "bna_swiglu", "bna_gemv_rmsnorm", "bna_gemv_gated",
     "bna_gemv", "bna_launch_probe", "bna_decode_step_qk", "bna_prefill_attention_gated",
-    "bna_gemm_swiglu", "bna_gemm_qkv_norm_rope", "bna_gemm_residual",
+    "bna_gemm_swiglu", "bna_gemm_qkv_norm_rope", "bna_gemm_residual", "bna_row_sumsq",
 )
 
 
@@ -81,10 +81,11 @@ def lib() -> ctypes.CDLL:
                                        i64, i32, i32, i32, f32, i32, vp]),
             "bna_gate_sigmoid_mul": (i32, [vp, vp, i64, i64, vp, i64, i32, i32, i32, vp]),
             "bna_swiglu": (i32, [vp, i64, i64, vp, i64, i32, i32, vp]),
-            "bna_gemm_swiglu": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, vp]),
+            "bna_gemm_swiglu": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, vp, i64, i32, f32, i32, vp]),
             "bna_gemm_qkv_norm_rope": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, vp, vp, vp, vp, i32,
-                                             f32, i32, vp]),
-            "bna_gemm_residual": (i32, [vp, i64, vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, vp]),
+                                             f32, vp, i64, i32, f32, i32, vp]),
+            "bna_row_sumsq": (i32, [vp, i64, vp, i64, i64, i32, i32, vp]),
+            "bna_gemm_residual": (i32, [vp, i64, vp, i64, vp, i64, vp, i64, i64, i32, i32, vp, i64, i32, vp]),
             "bna_gemv_rmsnorm": (i32, [vp, i64, vp, i64, vp, f32, vp, i64, vp, i64, i64, i32, vp, i64, i32, i32, vp]),
             "bna_gemv_gated": (i32, [vp, vp, i64, i64, i32, vp, i64, i64, vp, i64, vp, i64, i32, i32, vp]),
             "bna_launch_probe": (i32, [i32, vp]),

@@ -89,6 +89,17 @@ struct GemmArgs {
   // residual epilogue: out = round(acc + res), res [M, N] of row stride ldr (may be out)
   const uint8_t* res;
   int64_t ldr;
+  // residual epilogue: per-row partial sums of squares of the (rounded) output, [M, ss_ld]
+  // fp32 with column 4 * tn + part (a quarter of a 256-column tile each); null: none
+  float* ss_out;
+  int ss_ld;
+  // SwiGLU / q/k/v: RMSNorm folded in.  The A operand is the un-normalised residual, W carries
+  // the norm weight (1 + w) per column of K, and the accumulator of row m is scaled by
+  // rsqrt(sum(rs[m, 0:rs_parts]) * rs_inv_n + rs_eps) before the epilogue; null: no scaling
+  const float* rs;
+  int rs_parts;
+  int64_t rs_ld;
+  float rs_inv_n, rs_eps;
 };
 
 __device__ __forceinline__ void unpack8v(const uint4& u, float* f, bool bf) {
@@ -122,7 +133,7 @@ __device__ __forceinline__ float qk_norm1(float x, float r, float w) {
 // per thread (one full sector of the row).
 template <typename T>
 __device__ __forceinline__ void qkv_group_epilogue(const GemmArgs& a, uint32_t tg, uint8_t* orow, bool store,
-                                                   int kind, int64_t m, const uint8_t* norm_smem) {
+                                                   int kind, int64_t m, const uint8_t* norm_smem, float rsc) {
   using namespace sm100;
   constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
   const bool s256 = a.st256 != 0;
@@ -133,6 +144,8 @@ __device__ __forceinline__ void qkv_group_epilogue(const GemmArgs& a, uint32_t t
       tmem_ld16(tg + (uint32_t)c, x);
       tmem_ld16(tg + (uint32_t)(c + 16), x + 16);
       tmem_ld_wait();
+#pragma unroll
+      for (int e = 0; e < 32; ++e) x[e] *= rsc;
       uint32_t w[16];
 #pragma unroll
       for (int e = 0; e < 16; ++e) w[e] = ElemTraits<T>::pack2(x[2 * e], x[2 * e + 1]);
@@ -161,7 +174,7 @@ __device__ __forceinline__ void qkv_group_epilogue(const GemmArgs& a, uint32_t t
     tmem_ld_wait();
 #pragma unroll
     for (int e = 0; e < 32; ++e) {
-      const float v = round_to<T>(x[e]);
+      const float v = round_to<T>(x[e] * rsc);
       ss = fmaf(v, v, ss);
     }
   }
@@ -174,6 +187,11 @@ __device__ __forceinline__ void qkv_group_epilogue(const GemmArgs& a, uint32_t t
     tmem_ld16(tg + (uint32_t)c, x1);
     tmem_ld16(tg + (uint32_t)(c + hr), x2);
     tmem_ld_wait();
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      x1[e] *= rsc;
+      x2[e] *= rsc;
+    }
     uint32_t o1[8], o2[8];
 #pragma unroll
     for (int hb = 0; hb < 16; hb += 8) {
@@ -209,6 +227,8 @@ __device__ __forceinline__ void qkv_group_epilogue(const GemmArgs& a, uint32_t t
     float x[16];
     tmem_ld16(tg + (uint32_t)c, x);
     tmem_ld_wait();
+#pragma unroll
+    for (int e = 0; e < 16; ++e) x[e] *= rsc;
     uint32_t o[8];
 #pragma unroll
     for (int hb = 0; hb < 16; hb += 8) {
@@ -227,7 +247,7 @@ __device__ __forceinline__ void qkv_group_epilogue(const GemmArgs& a, uint32_t t
 // 128-column head groups), tn the tile's 256-column block.
 template <typename T, int EPI>
 __device__ __forceinline__ void tile_epilogue(const GemmArgs& a, uint32_t tacc, int m, int tn, int half,
-                                              const uint8_t* norm_smem, const uint4* rv) {
+                                              const uint8_t* norm_smem, const uint4* rv, float rsc) {
   using namespace sm100;
   if constexpr (EPI == kEpiSwiglu) {
     // warp part `half` (0..3) of the row: output columns [32 half, 32 half + 32)
@@ -242,9 +262,9 @@ __device__ __forceinline__ void tile_epilogue(const GemmArgs& a, uint32_t tacc, 
 #pragma unroll
       for (int e = 0; e < 16; e += 2) {
         // gate products rounded (as a pair), silu rounded, times the rounded up products
-        const float2 gr = ElemTraits<T>::unpack2(ElemTraits<T>::pack2(g[e], g[e + 1]));
+        const float2 gr = ElemTraits<T>::unpack2(ElemTraits<T>::pack2(g[e] * rsc, g[e + 1] * rsc));
         w[e >> 1] = ElemTraits<T>::mul2(ElemTraits<T>::pack2(silu_fast(gr.x), silu_fast(gr.y)),
-                                        ElemTraits<T>::pack2(u[e], u[e + 1]));
+                                        ElemTraits<T>::pack2(u[e] * rsc, u[e + 1] * rsc));
       }
       if (m < a.M) {
         if (a.st256) {
@@ -260,6 +280,7 @@ __device__ __forceinline__ void tile_epilogue(const GemmArgs& a, uint32_t tacc, 
     // holds the residual of those columns, loaded before the accumulator wait by the thread
     // that writes the sums (so in place is allowed)
     uint8_t* orow = a.out + 2 * ((int64_t)m * a.ldo + (int64_t)tn * 256 + half * 64);
+    float ss = 0.f;  // sum of squares of this thread's 64 outputs (the next norm's input)
 #pragma unroll
     for (int c = 0; c < 64; c += 16) {
       float x[16];
@@ -274,6 +295,9 @@ __device__ __forceinline__ void tile_epilogue(const GemmArgs& a, uint32_t tacc, 
         const float2 p2 = ElemTraits<T>::unpack2(ElemTraits<T>::pack2(x[2 * e], x[2 * e + 1]));
         const float2 r2 = ElemTraits<T>::unpack2(rw[e]);
         w[e] = ElemTraits<T>::pack2(p2.x + r2.x, p2.y + r2.y);
+        const float2 o2 = ElemTraits<T>::unpack2(w[e]);
+        ss = fmaf(o2.x, o2.x, ss);
+        ss = fmaf(o2.y, o2.y, ss);
       }
       if (m < a.M) {
         if (a.st256) {
@@ -284,11 +308,12 @@ __device__ __forceinline__ void tile_epilogue(const GemmArgs& a, uint32_t tacc, 
         }
       }
     }
+    if (a.ss_out && m < a.M) a.ss_out[(int64_t)m * a.ss_ld + 4 * tn + half] = ss;
   } else {
     const int grp = tn * 2 + half;  // 128-column head group of this warp
     const int kind = grp < a.q_groups ? ((grp & 1) ? 0 : 1) : (grp < a.q_groups + a.k_groups ? 2 : 0);
     qkv_group_epilogue<T>(a, tacc + (uint32_t)half * 128u, a.out + 2 * ((int64_t)m * a.ldo + grp * 128), m < a.M,
-                          kind, m < a.M ? m : 0, norm_smem);
+                          kind, m < a.M ? m : 0, norm_smem, rsc);
   }
 }
 
@@ -303,6 +328,19 @@ __device__ __forceinline__ void load_residual(const GemmArgs& a, int m, int tn, 
 #pragma unroll
     for (int i = 0; i < 8; ++i) rv[i] = make_uint4(0, 0, 0, 0);
   }
+}
+
+// Folded RMSNorm: the row scale of row m from the partial sums of squares (1 without them).
+__device__ __forceinline__ float row_scale(const GemmArgs& a, int m) {
+  if (!a.rs || m >= a.M) return 1.f;
+  const float* p = a.rs + (int64_t)m * a.rs_ld;
+  float s = 0.f;
+#pragma unroll 4
+  for (int i = 0; i < a.rs_parts; i += 4) {
+    const float4 v = *reinterpret_cast<const float4*>(p + i);
+    s += (v.x + v.y) + (v.z + v.w);
+  }
+  return rsqrtf(s * a.rs_inv_n + a.rs_eps);
 }
 
 template <typename T, int EPI>
@@ -428,9 +466,10 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
       const int m = (tile / a.tiles_n) * 128 + row, tn = tile % a.tiles_n;
       uint4 rv[EPI == kEpiResid ? 8 : 1];
       if constexpr (EPI == kEpiResid) load_residual(a, m, tn, half, rv);
+      const float rsc = EPI == kEpiResid ? 1.f : row_scale(a, m);
       if (!mbar_wait(&accfull[buf], (uint32_t)(tc >> 1) & 1u, abort_flag, 25, a.err)) break;
       tc_fence_after();
-      tile_epilogue<T, EPI>(a, tmem + lane_off + (uint32_t)buf * 256u, m, tn, half, smem + kNormOff, rv);
+      tile_epilogue<T, EPI>(a, tmem + lane_off + (uint32_t)buf * 256u, m, tn, half, smem + kNormOff, rv, rsc);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&accempty[buf]);
@@ -593,9 +632,10 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
       const int m = (tile / a.tiles_n) * 256 + (int)rank * 128 + row, tn = tile % a.tiles_n;
       uint4 rv[EPI == kEpiResid ? 8 : 1];
       if constexpr (EPI == kEpiResid) load_residual(a, m, tn, half, rv);
+      const float rsc = EPI == kEpiResid ? 1.f : row_scale(a, m);
       if (!mbar_wait(&accfull[buf], (uint32_t)(tc >> 1) & 1u, abort_flag, 35, a.err)) break;
       tc_fence_after();
-      tile_epilogue<T, EPI>(a, tmem + lane_off + (uint32_t)buf * 256u, m, tn, half, smem + kPairNormOff, rv);
+      tile_epilogue<T, EPI>(a, tmem + lane_off + (uint32_t)buf * 256u, m, tn, half, smem + kPairNormOff, rv, rsc);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(accempty0 + (uint32_t)buf * 8u);
@@ -744,14 +784,33 @@ int check_gemm_common(const void* h, int64_t ldh, const void* w, int64_t ldw, co
   return BNA_OK;
 }
 
+// Folded-RMSNorm arguments of the SwiGLU and q/k/v GEMMs (row_ss null: none).
+int set_row_scale(GemmArgs& a, const float* row_ss, int64_t ld, int32_t parts, float eps, int K, const char* name) {
+  if (!row_ss) return BNA_OK;
+  const std::string n(name);
+  if (parts <= 0 || parts % 4 || ld < parts || ld % 4 || (reinterpret_cast<uintptr_t>(row_ss) & 15))
+    return fail(BNA_BAD_STRIDE, n + ": row sums of squares need a positive multiple of 4 parts, a row stride of 4 floats and 16-byte alignment");
+  a.rs = row_ss;
+  a.rs_ld = ld;
+  a.rs_parts = parts;
+  a.rs_inv_n = 1.f / (float)K;
+  a.rs_eps = eps;
+  return BNA_OK;
+}
+
 }  // namespace
 }  // namespace bna
 
 extern "C" BNA_API int bna_gemm_swiglu(const void* h, int64_t ldh, const void* w, int64_t ldw, void* out, int64_t ldo,
-                                       int64_t M, int32_t K, int32_t inter, int32_t dtype, void* stream) {
+                                       int64_t M, int32_t K, int32_t inter, const float* row_ss, int64_t row_ss_ld,
+                                       int32_t row_ss_parts, float norm_eps, int32_t dtype, void* stream) {
   if (int rc = check_gemm_common(h, ldh, w, ldw, out, ldo, M, K, dtype, "gemm_swiglu")) return rc;
   if (inter <= 0 || inter % 128) return fail(BNA_UNSUPPORTED, "gemm_swiglu: inter must be a positive multiple of 128");
   if (ldo < inter) return fail(BNA_BAD_STRIDE, "gemm_swiglu: output row stride below inter");
+  {
+    GemmArgs probe{};
+    if (int rc = set_row_scale(probe, row_ss, row_ss_ld, row_ss_parts, norm_eps, K, "gemm_swiglu")) return rc;
+  }
   if (M == 0) return BNA_OK;
   const CUtensorMapDataType dt = dtype == BNA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap ma, mw;
@@ -766,6 +825,7 @@ extern "C" BNA_API int bna_gemm_swiglu(const void* h, int64_t ldh, const void* w
   a.tile_w = 128;
   a.out = static_cast<uint8_t*>(out);
   a.ldo = ldo;
+  if (int rc = set_row_scale(a, row_ss, row_ss_ld, row_ss_parts, norm_eps, K, "gemm_swiglu")) return rc;
   a.st256 = ((reinterpret_cast<uintptr_t>(out) & 31) == 0 && (ldo * 2) % 32 == 0) ? 1 : 0;
   return launch_gemm(kEpiSwiglu, ma, mw, a, dtype, stream);
 }
@@ -773,8 +833,9 @@ extern "C" BNA_API int bna_gemm_swiglu(const void* h, int64_t ldh, const void* w
 extern "C" BNA_API int bna_gemm_qkv_norm_rope(const void* h, int64_t ldh, const void* w, int64_t ldw, void* out,
                                               int64_t ldo, int64_t M, int32_t K, int32_t N, int32_t num_q_heads,
                                               int32_t num_kv_heads, const void* q_norm_w, const void* k_norm_w,
-                                              const void* cos, const void* sin, int32_t rot, float eps, int32_t dtype,
-                                              void* stream) {
+                                              const void* cos, const void* sin, int32_t rot, float eps,
+                                              const float* row_ss, int64_t row_ss_ld, int32_t row_ss_parts,
+                                              float norm_eps, int32_t dtype, void* stream) {
   if (int rc = check_gemm_common(h, ldh, w, ldw, out, ldo, M, K, dtype, "gemm_qkv_norm_rope")) return rc;
   if (N <= 0 || N % 256) return fail(BNA_UNSUPPORTED, "gemm_qkv_norm_rope: N must be a positive multiple of 256");
   if (ldo < N) return fail(BNA_BAD_STRIDE, "gemm_qkv_norm_rope: output row stride below N");
@@ -786,6 +847,10 @@ extern "C" BNA_API int bna_gemm_qkv_norm_rope(const void* h, int64_t ldh, const 
   if ((reinterpret_cast<uintptr_t>(q_norm_w) | reinterpret_cast<uintptr_t>(k_norm_w) | reinterpret_cast<uintptr_t>(cos) |
        reinterpret_cast<uintptr_t>(sin)) & 15)
     return fail(BNA_BAD_STRIDE, "gemm_qkv_norm_rope: norm weights and rotary tables must be 16-byte aligned");
+  {
+    GemmArgs probe{};
+    if (int rc = set_row_scale(probe, row_ss, row_ss_ld, row_ss_parts, norm_eps, K, "gemm_qkv_norm_rope")) return rc;
+  }
   if (M == 0) return BNA_OK;
   const CUtensorMapDataType dt = dtype == BNA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap ma, mw;
@@ -808,13 +873,14 @@ extern "C" BNA_API int bna_gemm_qkv_norm_rope(const void* h, int64_t ldh, const 
   a.sn = static_cast<const uint8_t*>(sin);
   a.rot = rot;
   a.eps = eps;
+  if (int rc = set_row_scale(a, row_ss, row_ss_ld, row_ss_parts, norm_eps, K, "gemm_qkv_norm_rope")) return rc;
   a.st256 = ((reinterpret_cast<uintptr_t>(out) & 31) == 0 && (ldo * 2) % 32 == 0) ? 1 : 0;
   return launch_gemm(kEpiQKNorm, ma, mw, a, dtype, stream);
 }
 
 extern "C" BNA_API int bna_gemm_residual(const void* h, int64_t ldh, const void* w, int64_t ldw, const void* res,
                                          int64_t ldr, void* out, int64_t ldo, int64_t M, int32_t K, int32_t N,
-                                         int32_t dtype, void* stream) {
+                                         float* ss_out, int64_t ss_ld, int32_t dtype, void* stream) {
   if (int rc = check_gemm_common(h, ldh, w, ldw, out, ldo, M, K, dtype, "gemm_residual")) return rc;
   if (N <= 0 || N % 256) return fail(BNA_UNSUPPORTED, "gemm_residual: N must be a positive multiple of 256");
   if (ldo < N || ldr < N) return fail(BNA_BAD_STRIDE, "gemm_residual: output / residual row stride below N");
@@ -826,6 +892,8 @@ extern "C" BNA_API int bna_gemm_residual(const void* h, int64_t ldh, const void*
     const uintptr_t r1 = r0 + 2 * (uintptr_t)((M - 1) * ldr + N), o1 = o0 + 2 * (uintptr_t)((M - 1) * ldo + N);
     if (M > 0 && r0 < o1 && o0 < r1) return fail(BNA_BAD_SHAPE, "gemm_residual: residual overlaps the output other than in place");
   }
+  if (ss_out && (ss_ld < 4 * (N / 256) || ss_ld % 4 || (reinterpret_cast<uintptr_t>(ss_out) & 15)))
+    return fail(BNA_BAD_STRIDE, "gemm_residual: ss_out needs a row stride of at least 4 * N / 256 floats, a multiple of 4, 16-byte aligned");
   if (M == 0) return BNA_OK;
   const CUtensorMapDataType dt = dtype == BNA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap ma, mw;
@@ -841,6 +909,8 @@ extern "C" BNA_API int bna_gemm_residual(const void* h, int64_t ldh, const void*
   a.ldo = ldo;
   a.res = static_cast<const uint8_t*>(res);
   a.ldr = ldr;
+  a.ss_out = ss_out;
+  a.ss_ld = (int)ss_ld;
   a.st256 = ((reinterpret_cast<uintptr_t>(out) & 31) == 0 && (ldo * 2) % 32 == 0) ? 1 : 0;
   return launch_gemm(kEpiResid, ma, mw, a, dtype, stream);
 }

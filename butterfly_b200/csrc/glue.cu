@@ -311,10 +311,48 @@ int launch_rmsnorm(const NormArgs& a, cudaStream_t s) {
   return check_cuda(cudaGetLastError(), "rmsnorm launch");
 }
 
+// Sum of squares of each row (fp32), one warp per row: the statistics of an RMSNorm that a
+// following GEMM applies as a row scale (bna_gemm_swiglu / bna_gemm_qkv_norm_rope row_ss).
+template <typename T>
+__global__ void __launch_bounds__(256) row_sumsq_kernel(const uint8_t* x, int64_t xs, float* out, int64_t ld,
+                                                        int64_t rows, int H) {
+  constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
+  const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const uint8_t* row = x + 2 * r * xs;
+  float ss = 0.f;
+  for (int c = lane * 8; c < H; c += 256) {
+    float f[8];
+    unpack8(ld_nc_128(row + 2 * c), f, bf);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) *reinterpret_cast<float4*>(out + r * ld) = make_float4(ss, 0.f, 0.f, 0.f);
+}
+
 }  // namespace
 }  // namespace bna
 
 using namespace bna;
+
+extern "C" BNA_API int bna_row_sumsq(const void* x, int64_t x_stride, float* out, int64_t ld_out, int64_t rows,
+                                     int32_t H, int32_t dtype, void* stream) {
+  if (rows < 0 || H <= 0 || H % 8) return fail(BNA_BAD_SHAPE, "row_sumsq: rows >= 0 and H a positive multiple of 8");
+  if (rows == 0) return BNA_OK;
+  if (!x || !out) return fail(BNA_BAD_SHAPE, "row_sumsq: null pointer");
+  if (dtype != BNA_BF16 && dtype != BNA_F16) return fail(BNA_BAD_DTYPE, "row_sumsq: bfloat16 or float16 only");
+  if (x_stride % 8 || ld_out < 4 || ld_out % 4 || !aligned16(x) || !aligned16(out))
+    return fail(BNA_BAD_STRIDE, "row_sumsq: 16-byte aligned rows (stride a multiple of 8 elements), ld_out a multiple of 4 floats");
+  const dim3 grid((unsigned)((rows + 7) / 8)), block(256);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint8_t* xp = static_cast<const uint8_t*>(x);
+  if (dtype == BNA_BF16) row_sumsq_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(xp, x_stride, out, ld_out, rows, H);
+  else row_sumsq_kernel<__half><<<grid, block, 0, s>>>(xp, x_stride, out, ld_out, rows, H);
+  return check_cuda(cudaGetLastError(), "row_sumsq launch");
+}
 
 extern "C" BNA_API int bna_rmsnorm(const void* x, int64_t x_stride, const void* res, int64_t res_stride,
                                    const void* weight, void* out, int64_t out_stride, void* sum_out,

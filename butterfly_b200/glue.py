@@ -147,10 +147,36 @@ def swiglu(gate_up: torch.Tensor, inter: int) -> torch.Tensor:
     return out
 
 
-def gemm_swiglu(h: torch.Tensor, w_gate_up: torch.Tensor, inter: int) -> torch.Tensor:
+def _row_ss_args(row_ss: Optional[torch.Tensor], rows: int, eps: float):
+    """(pointer, row stride, parts, eps) of per-row partial sums of squares [rows, parts] fp32."""
+    if row_ss is None:
+        return None, 0, 0, 0.0
+    if (row_ss.dtype != torch.float32 or row_ss.dim() != 2 or int(row_ss.shape[0]) != rows or row_ss.stride(1) != 1
+            or row_ss.device.type != "cuda"):
+        raise ValueError(f"row_ss must be a [{rows}, parts] float32 CUDA tensor with a contiguous last dim")
+    return row_ss.data_ptr(), int(row_ss.stride(0)), int(row_ss.shape[1]), float(eps)
+
+
+def row_sumsq(x: torch.Tensor) -> torch.Tensor:
+    """Per-row sums of squares of x [..., H] as a [rows, 4] float32 tensor (the sum in column 0):
+    the ``row_ss`` of the folded-RMSNorm GEMMs for rows no residual GEMM produced."""
+    _lib.require_cuda(x)
+    H = int(x.shape[-1])
+    rows, xs = _rows(x, H)
+    out = torch.empty((rows, 4), device=x.device, dtype=torch.float32)
+    _lib.check(_lib.lib().bna_row_sumsq(x.data_ptr(), xs, out.data_ptr(), 4, rows, H, _lib.dtype_code(x.dtype),
+                                        _lib.stream_ptr(x.device)))
+    return out
+
+
+def gemm_swiglu(h: torch.Tensor, w_gate_up: torch.Tensor, inter: int, row_ss: Optional[torch.Tensor] = None,
+                norm_eps: float = 0.0) -> torch.Tensor:
     """silu(h @ Wg^T) * (h @ Wu^T) for h [..., K] and w_gate_up [2*inter, K] = [Wg; Wu], on
     the tcgen05 GEMM with SwiGLU in its epilogue -> [..., inter] (the [.., 2*inter]
-    product never reaches HBM)."""
+    product never reaches HBM).  With ``row_ss`` (per-row partial sums of squares of h,
+    [rows, parts] float32) the RMSNorm before the MLP is folded in: h is un-normalised, the
+    norm weight (1 + w) is already in w_gate_up's columns, and row m's products are scaled
+    by rsqrt(sum(row_ss[m]) / K + norm_eps)."""
     _lib.require_cuda(h, w_gate_up)
     K = int(h.shape[-1])
     rows, ldh = _rows(h, K)
@@ -159,19 +185,21 @@ def gemm_swiglu(h: torch.Tensor, w_gate_up: torch.Tensor, inter: int) -> torch.T
     if w_gate_up.stride(1) != 1 or w_gate_up.dtype != h.dtype:
         raise ValueError("w_gate_up must be row-major with h's dtype")
     out = torch.empty((*h.shape[:-1], inter), device=h.device, dtype=h.dtype)
+    rp, rl, rn, re = _row_ss_args(row_ss, rows, norm_eps)
     _lib.check(_lib.lib().bna_gemm_swiglu(h.data_ptr(), ldh, w_gate_up.data_ptr(), w_gate_up.stride(0),
-                                          out.data_ptr(), inter, rows, K, inter, _lib.dtype_code(h.dtype),
-                                          _lib.stream_ptr(h.device)))
+                                          out.data_ptr(), inter, rows, K, inter, rp, rl, rn, re,
+                                          _lib.dtype_code(h.dtype), _lib.stream_ptr(h.device)))
     return out
 
 
 def gemm_qkv_norm_rope(h: torch.Tensor, w_qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int,
                        q_weight: torch.Tensor, k_weight: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
-                       eps: float) -> torch.Tensor:
+                       eps: float, row_ss: Optional[torch.Tensor] = None, norm_eps: float = 0.0) -> torch.Tensor:
     """h [B,T,K] @ w_qkv^T on the tcgen05 GEMM, w_qkv [N, K] the merged gated q_proj, k_proj and
     v_proj rows (per query head 128 query then 128 gate rows; N = (2 Hq + 2 Hkv) * 128), with
     the q/k RMSNorm and the rotary embedding (cos/sin [B,T,rot] or [1,T,rot]) applied to the
-    query and key columns in the epilogue -> [B,T,N] (the layout the projection had)."""
+    query and key columns in the epilogue -> [B,T,N] (the layout the projection had).
+    ``row_ss`` / ``norm_eps`` fold the layer's input RMSNorm in, as for ``gemm_swiglu``."""
     _lib.require_cuda(h, w_qkv, q_weight, k_weight, cos, sin)
     B, T, K = h.shape
     N = int(w_qkv.shape[0])
@@ -189,16 +217,18 @@ def gemm_qkv_norm_rope(h: torch.Tensor, w_qkv: torch.Tensor, num_q_heads: int, n
     _lib.check(_lib.lib().bna_gemm_qkv_norm_rope(
         h.data_ptr(), ldh, w_qkv.data_ptr(), w_qkv.stride(0), out.data_ptr(), N, rows, K, N, int(num_q_heads),
         int(num_kv_heads), q_weight.data_ptr(), k_weight.data_ptr(), cs.data_ptr(), sn.data_ptr(), rot, float(eps),
-        _lib.dtype_code(h.dtype), _lib.stream_ptr(h.device)))
+        *_row_ss_args(row_ss, rows, norm_eps), _lib.dtype_code(h.dtype), _lib.stream_ptr(h.device)))
     return out
 
 
 def gemm_residual(h: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
-                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                  out: Optional[torch.Tensor] = None, ss_out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """residual + h @ w^T for h [..., K], w [N, K] row-major and residual [..., N] with the
     eager ops' rounding (the projection rounded, then the sum), on the tcgen05 GEMM with the
     residual add in its epilogue.
-    ``out`` may be ``residual`` itself (an in-place add, as ``residual.addmm_``)."""
+    ``out`` may be ``residual`` itself (an in-place add, as ``residual.addmm_``).  ``ss_out``
+    ([rows, >= 4 N / 256] float32) receives per-row partial sums of squares of the output,
+    the ``row_ss`` of a following folded-RMSNorm GEMM."""
     _lib.require_cuda(h, w, residual)
     K = int(h.shape[-1])
     N = int(w.shape[0])
@@ -213,8 +243,14 @@ def gemm_residual(h: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
     elif tuple(out.shape) != tuple(residual.shape) or out.dtype != h.dtype:
         raise ValueError("out must match residual")
     ro, ldo = _rows(out, N)
+    sp, sl = None, 0
+    if ss_out is not None:
+        if (ss_out.dtype != torch.float32 or ss_out.dim() != 2 or int(ss_out.shape[0]) != rows
+                or int(ss_out.shape[1]) < 4 * (N // 256) or ss_out.stride(1) != 1 or ss_out.device != h.device):
+            raise ValueError(f"ss_out must be a [{rows}, >= {4 * (N // 256)}] float32 tensor on h's device")
+        sp, sl = ss_out.data_ptr(), int(ss_out.stride(0))
     _lib.check(_lib.lib().bna_gemm_residual(h.data_ptr(), ldh, w.data_ptr(), w.stride(0), residual.data_ptr(), ldr,
-                                            out.data_ptr(), ldo, rows, K, N, _lib.dtype_code(h.dtype),
+                                            out.data_ptr(), ldo, rows, K, N, sp, sl, _lib.dtype_code(h.dtype),
                                             _lib.stream_ptr(h.device)))
     return out
 

@@ -84,6 +84,30 @@ class _FusedState:
         hidden = src.o_proj.out_features
         self.gemm_resid = (hidden % 256 == 0 and src.o_proj.in_features % 64 == 0 and self.inter % 64 == 0
                            and mlp.down_proj.out_features == hidden)
+        # with all three, the two RMSNorms fold into the GEMMs after them (weights with the norm
+        # weight folded in, cached against both tensors' version counters)
+        self.fold_norms = self.gemm_qkv and self.gemm_swiglu and self.gemm_resid
+        self._folded: dict = {}
+
+    def folded(self, key: str, norm_weight: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """w with the Qwen3.5 RMSNorm weight folded into its columns: round(w[:, k] * (1 + g[k])).
+        Recomputed whenever either tensor changes in place (a weight load)."""
+        ver = (norm_weight.data_ptr(), norm_weight._version, w.data_ptr(), w._version)
+        hit = self._folded.get(key)
+        if hit is None or hit[0] != ver:
+            f = (w.float() * (1.0 + norm_weight.float())[None, :]).to(w.dtype)
+            self._folded[key] = (ver, f)
+            return f
+        return hit[1]
+
+
+def _row_stats(x: torch.Tensor, rows: int) -> torch.Tensor:
+    """Per-row partial sums of squares of the residual stream x: the ones the previous layer's
+    down projection wrote (still valid for this storage and version), else computed."""
+    t = getattr(x, "_bna_row_ss", None)
+    if t is not None and t[1] == x.data_ptr() and t[2] == x._version and int(t[0].shape[0]) == rows:
+        return t[0]
+    return glue.row_sumsq(x)
 
 
 def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=None, attention_mask=None,
@@ -108,7 +132,12 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
     cos, sin = position_embeddings
     # whole-prompt / chunk prefill: q/k norm + RoPE in the q/k/v GEMM's epilogue
     prepped = (not decode and attn._shard is None and st.gemm_qkv and int(cos.shape[-1]) % 32 == 0)
-    if not decode:
+    fold = prepped and st.fold_norms
+    if fold:  # the input RMSNorm folded into the q/k/v GEMM (row statistics, folded weights)
+        qkv = glue.gemm_qkv_norm_rope(x, st.folded("qkv", self.input_layernorm.weight, st.w_qkv), hq, hkv,
+                                      src.q_norm.weight, src.k_norm.weight, cos, sin, src.q_norm.eps,
+                                      row_ss=_row_stats(x, B * T), norm_eps=self.input_layernorm.eps)
+    elif not decode:
         h = glue.rmsnorm(x, self.input_layernorm.weight, self.input_layernorm.eps)
         if prepped:
             qkv = glue.gemm_qkv_norm_rope(h, st.w_qkv, hq, hkv, src.q_norm.weight, src.k_norm.weight, cos, sin,
@@ -162,6 +191,18 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
         y = glue.gate_sigmoid_mul(out.transpose(1, 2), qg[..., dh:])  # out storage is [B,T,hq,dh]
     else:
         y = gated
+    if fold:
+        # o_proj + residual (writing the row statistics), gate/up with the post-attention norm
+        # folded in, down_proj accumulated in place (writing the next layer's statistics)
+        rs2 = torch.empty((B * T, 4 * (H // 256)), device=x.device, dtype=torch.float32)
+        x2 = glue.gemm_residual(y, src.o_proj.weight, x, ss_out=rs2)
+        act = glue.gemm_swiglu(x2, st.folded("gu", self.post_attention_layernorm.weight, st.w_gu), st.inter,
+                               row_ss=rs2, norm_eps=self.post_attention_layernorm.eps)
+        rs3 = torch.empty_like(rs2)
+        glue.gemm_residual(act, self.mlp.down_proj.weight, x2, out=x2, ss_out=rs3)
+        x2._bna_row_ss = (rs3, x2.data_ptr(), x2._version)
+        attn._profile(T, k_len_after, backend, hit, t0, fused=True)
+        return x2
     if st.gemm_resid:  # o_proj with the residual add in the epilogue, then the norm
         x2 = glue.gemm_residual(y, src.o_proj.weight, x)
         h2 = glue.rmsnorm(x2, self.post_attention_layernorm.weight, self.post_attention_layernorm.eps)

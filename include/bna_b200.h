@@ -250,9 +250,15 @@ BNA_API int bna_swiglu(const void* gate_up, int64_t row_stride, int64_t up_offse
  * [M, inter] (row stride ldo), all row-major.  The gate and up products, silu(gate) and the
  * product are each rounded to the 16-bit type, as the eager ops (transformers'
  * Qwen3_5MLP: act_fn(gate_proj(x)) * up_proj(x)); accumulation is fp32.  K a multiple of 64,
- * inter of 128, row strides multiples of 8 elements, pointers 16-byte aligned. */
+ * inter of 128, row strides multiples of 8 elements, pointers 16-byte aligned.
+ * With row_ss non-NULL the MLP's RMSNorm is folded in: h is the un-normalised residual, w
+ * carries the norm weight (1 + w_norm[k]) in column k, and row m's products are scaled by
+ * rsqrt(sum(row_ss[m * row_ss_ld + 0 .. row_ss_parts)) / K + norm_eps) before rounding
+ * (row_ss: fp32 partial sums of squares of the row, from bna_gemm_residual's ss_out or
+ * bna_row_sumsq; row_ss_parts a multiple of 4). */
 BNA_API int bna_gemm_swiglu(const void* h, int64_t ldh, const void* w, int64_t ldw, void* out, int64_t ldo,
-                            int64_t M, int32_t K, int32_t inter, int32_t dtype, void* stream);
+                            int64_t M, int32_t K, int32_t inter, const float* row_ss, int64_t row_ss_ld,
+                            int32_t row_ss_parts, float norm_eps, int32_t dtype, void* stream);
 
 /* The merged q/k/v projection with the q/k RMSNorm and rotary embedding in the epilogue:
  * out[m, :] = h[m,:] . w^T for w [N, K] whose rows come in 128-row head groups
@@ -261,11 +267,13 @@ BNA_API int bna_gemm_swiglu(const void* h, int64_t ldh, const void* w, int64_t l
  * normalised (Qwen3.5 RMSNorm, weights q_norm_w / k_norm_w [128]) and rotated in
  * rotate-half form on its first `rot` dims with cos / sin [M, rot] (row m's tables),
  * the rounding steps of the eager ops (bna_qk_norm_rope); gate and value groups are the
- * rounded products.  K a multiple of 64, rot a multiple of 32. */
+ * rounded products.  K a multiple of 64, rot a multiple of 32.  row_ss / row_ss_ld /
+ * row_ss_parts / norm_eps fold the layer's input RMSNorm in, as for bna_gemm_swiglu. */
 BNA_API int bna_gemm_qkv_norm_rope(const void* h, int64_t ldh, const void* w, int64_t ldw, void* out, int64_t ldo,
                                    int64_t M, int32_t K, int32_t N, int32_t num_q_heads, int32_t num_kv_heads,
                                    const void* q_norm_w, const void* k_norm_w, const void* cos, const void* sin,
-                                   int32_t rot, float eps, int32_t dtype, void* stream);
+                                   int32_t rot, float eps, const float* row_ss, int64_t row_ss_ld,
+                                   int32_t row_ss_parts, float norm_eps, int32_t dtype, void* stream);
 
 /* A projection followed by the decoder layer's residual add, on tcgen05 tensor cores:
  * out[m, n] = round(round(h[m,:] . w[n,:]) + res[m, n]) for m < M, n < N: the projection
@@ -273,9 +281,18 @@ BNA_API int bna_gemm_qkv_norm_rope(const void* h, int64_t ldh, const void* w, in
  * Qwen3_5DecoderLayer (residual + o_proj(attn), residual + down_proj(mlp); qwen_torch.py
  * :1585-1591 feeds o_proj).  out may be res
  * (same pointer and row stride: an in-place add); any other overlap is rejected.  K a
- * multiple of 64, N of 256, row strides multiples of 8 elements, pointers 16-byte aligned. */
+ * multiple of 64, N of 256, row strides multiples of 8 elements, pointers 16-byte aligned.
+ * With ss_out non-NULL, ss_out[m * ss_ld + 4 t + p] receives the fp32 sum of squares of the
+ * rounded outputs of row m in columns [256 t + 64 p, +64) (ss_ld >= 4 N / 256): the next
+ * RMSNorm's statistics, for the row_ss argument of the SwiGLU and q/k/v GEMMs. */
 BNA_API int bna_gemm_residual(const void* h, int64_t ldh, const void* w, int64_t ldw, const void* res, int64_t ldr,
-                              void* out, int64_t ldo, int64_t M, int32_t K, int32_t N, int32_t dtype, void* stream);
+                              void* out, int64_t ldo, int64_t M, int32_t K, int32_t N, float* ss_out, int64_t ss_ld,
+                              int32_t dtype, void* stream);
+
+/* out[r * ld_out + 0..3] = {sum_k x[r, k]^2, 0, 0, 0} in fp32 for r < rows, k < H: the
+ * row_ss input (4 parts) of the folded-RMSNorm GEMMs for rows no residual GEMM produced. */
+BNA_API int bna_row_sumsq(const void* x, int64_t x_stride, float* out, int64_t ld_out, int64_t rows, int32_t H,
+                          int32_t dtype, void* stream);
 
 /* Decode-time projections for 1..8 tokens (y = W x per token, W [out_features,
  * in_features] row-major, in_features a multiple of 256), with the layer step before the

@@ -81,7 +81,11 @@ def test_decode_step_qk_rejections():
 
 
 def test_gemm_rejections():
-    sw = L().bna_gemm_swiglu
+    raw = L().bna_gemm_swiglu
+
+    def sw(h, ldh, w, ldw, out, ldo, M, K, inter, dt, s, rs=None, rs_ld=0, rs_parts=0):
+        return raw(h, ldh, w, ldw, out, ldo, M, K, inter, rs, rs_ld, rs_parts, 1e-6, dt, s)
+
     assert sw(P, 1024, P, 1024, P, 3584, 0, 1024, 3584, BF, None) == OK          # no rows: no launch
     assert sw(P, 1024, P, 1024, P, 3584, 8, 1000, 3584, BF, None) == UNSUPPORTED  # K % 64
     assert sw(P, 1024, P, 1024, P, 3584, 8, 1024, 3500, BF, None) == UNSUPPORTED  # inter % 128
@@ -89,11 +93,15 @@ def test_gemm_rejections():
     assert sw(P + 2, 1024, P, 1024, P, 3584, 8, 1024, 3584, BF, None) == BAD_STRIDE
     assert sw(P, 1000, P, 1024, P, 3584, 8, 1024, 3584, BF, None) == BAD_STRIDE     # ldh < K
     assert sw(None, 1024, P, 1024, P, 3584, 8, 1024, 3584, BF, None) == BAD_SHAPE
+    # folded RMSNorm statistics: parts a positive multiple of 4 within the row stride, aligned
+    assert sw(P, 1024, P, 1024, P, 3584, 8, 1024, 3584, BF, None, P, 16, 6) == BAD_STRIDE
+    assert sw(P, 1024, P, 1024, P, 3584, 8, 1024, 3584, BF, None, P, 8, 16) == BAD_STRIDE
+    assert sw(P, 1024, P, 1024, P, 3584, 8, 1024, 3584, BF, None, P + 4, 16, 16) == BAD_STRIDE
     qk = L().bna_gemm_qkv_norm_rope
 
     def q(**kw):
         a = dict(h=P, ldh=1024, w=P, ldw=1024, out=P, ldo=2560, M=8, K=1024, N=2560, hq=8, hkv=2, qw=P, kw=P,
-                 cos=P, sin=P, rot=32, eps=1e-6, dt=BF, s=None)
+                 cos=P, sin=P, rot=32, eps=1e-6, rs=None, rs_ld=0, rs_parts=0, rs_eps=0.0, dt=BF, s=None)
         a.update(kw)
         return qk(*a.values())
 
@@ -104,6 +112,26 @@ def test_gemm_rejections():
     assert q(qw=None) == BAD_SHAPE
     assert q(cos=P + 8) == BAD_STRIDE
     assert q(ldo=2048) == BAD_STRIDE
+    assert q(rs=P, rs_ld=4, rs_parts=0) == BAD_STRIDE
+    res = L().bna_gemm_residual
+
+    def rr(**kw):
+        a = dict(h=P, ldh=1024, w=P, ldw=1024, r=P + 4096, ldr=1024, out=P + (1 << 30), ldo=1024, M=8, K=1024, N=1024,
+                 ss=None, ss_ld=0, dt=BF, s=None)
+        a.update(kw)
+        return res(*a.values())
+
+    assert rr(M=0) == OK
+    assert rr(N=1000) == UNSUPPORTED
+    assert rr(r=None) == BAD_SHAPE
+    assert rr(ldr=1000) == BAD_STRIDE
+    assert rr(out=P + 4096 + 2048) == BAD_SHAPE      # partial overlap with the residual
+    assert rr(ss=P, ss_ld=8) == BAD_STRIDE            # fewer than 4 * N / 256 partial sums per row
+    rs = L().bna_row_sumsq
+    assert rs(P, 1024, P, 4, 0, 1024, BF, None) == OK
+    assert rs(P, 1024, P, 4, 8, 1001, BF, None) == BAD_SHAPE
+    assert rs(P, 1024, P, 2, 8, 1024, BF, None) == BAD_STRIDE
+    assert rs(P, 1024, P, 4, 8, 1024, 7, None) == BAD_DTYPE
 
 
 def test_prefill_gated_rejects_null_gate():

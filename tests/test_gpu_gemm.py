@@ -132,3 +132,63 @@ def test_gemm_residual_strided_and_rejects_partial_overlap():
     buf = torch.zeros(601, 1024, device="cuda").bfloat16()
     with pytest.raises(ValueError):
         glue.gemm_residual(torch.randn(600, 1024, device="cuda").bfloat16(), w, buf[:600], out=buf[1:])
+
+
+def _norm32(x, g, eps):
+    xf = x.float()
+    return xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * (1 + g.float())
+
+
+@pytest.mark.parametrize("M,K,inter", [(1000, 1024, 3584), (4096, 2560, 9728)])
+def test_gemm_swiglu_folded_rmsnorm(M, K, inter):
+    """The MLP's RMSNorm folded into the gate/up GEMM (row statistics + (1 + w) in the weight
+    columns) against the unfolded path (RMSNorm kernel, then the GEMM): both within the same
+    distance of the fp32 reference."""
+    g = torch.Generator(device="cuda").manual_seed(M + inter)
+    x = (torch.randn(M, K, device="cuda", generator=g) * 3).bfloat16()
+    nw = (torch.randn(K, device="cuda", generator=g) * 0.2).bfloat16()
+    w = (torch.randn(2 * inter, K, device="cuda", generator=g) / K ** 0.5).bfloat16()
+    eps = 1e-6
+    wf = (w.float() * (1 + nw.float())[None]).bfloat16()
+    got = glue.gemm_swiglu(x, wf, inter, row_ss=glue.row_sumsq(x), norm_eps=eps)
+    ref16 = glue.gemm_swiglu(glue.rmsnorm(x, nw, eps), w, inter)
+    n32 = _norm32(x, nw, eps)
+    ref32 = F.silu(n32 @ w[:inter].float().t()) * (n32 @ w[inter:].float().t())
+    scale = float(ref32.abs().max())
+    assert float((got.float() - ref16.float()).abs().max()) <= 0.03 * scale
+    e_got = float((got.float() - ref32).abs().max())
+    e_ref = float((ref16.float() - ref32).abs().max())
+    assert e_got <= e_ref + 0.01 * scale, (e_got, e_ref, scale)
+
+
+def test_gemm_qkv_folded_rmsnorm_and_residual_statistics():
+    """Input RMSNorm folded into the q/k/v GEMM, with the row statistics written by the
+    residual GEMM that produced its input (bna_gemm_residual ss_out), against the unfolded
+    path; and the statistics themselves against torch."""
+    g = torch.Generator(device="cuda").manual_seed(11)
+    T, K, Hq, Hkv, dh, rot = 3000, 1024, 8, 2, 128, 32
+    N = (2 * Hq + 2 * Hkv) * dh
+    a = torch.randn(T, 2048, device="cuda", generator=g).bfloat16()
+    wo = (torch.randn(K, 2048, device="cuda", generator=g) / 2048 ** 0.5).bfloat16()
+    res = torch.randn(T, K, device="cuda", generator=g).bfloat16()
+    ss = torch.empty(T, 16, device="cuda", dtype=torch.float32)
+    x = glue.gemm_residual(a, wo, res, ss_out=ss)
+    want = x.float().pow(2).sum(-1)
+    assert torch.allclose(ss.sum(-1), want, rtol=1e-4, atol=1e-3)
+    assert torch.allclose(glue.row_sumsq(x)[:, 0], want, rtol=1e-4, atol=1e-3)
+    nw = (torch.randn(K, device="cuda", generator=g) * 0.2).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).bfloat16()
+    qw = (torch.randn(dh, device="cuda", generator=g) * 0.1).bfloat16()
+    kw = (torch.randn(dh, device="cuda", generator=g) * 0.1).bfloat16()
+    pos = torch.arange(T, device="cuda", dtype=torch.float32)
+    inv = 1.0 / (10000 ** (torch.arange(0, rot, 2, device="cuda", dtype=torch.float32) / rot))
+    fr = torch.cat([pos[:, None] * inv[None], pos[:, None] * inv[None]], -1)
+    cos, sin = fr.cos()[None].bfloat16(), fr.sin()[None].bfloat16()
+    wf = (w.float() * (1 + nw.float())[None]).bfloat16()
+    got = glue.gemm_qkv_norm_rope(x.view(1, T, K), wf, Hq, Hkv, qw, kw, cos, sin, 1e-6, row_ss=ss, norm_eps=1e-6)
+    ref = glue.gemm_qkv_norm_rope(glue.rmsnorm(x, nw, 1e-6).view(1, T, K), w, Hq, Hkv, qw, kw, cos, sin, 1e-6)
+    for lo, hi in ((0, 2 * Hq * dh), (2 * Hq * dh, N)):
+        d = (got[..., lo:hi].float() - ref[..., lo:hi].float()).abs()
+        scale = float(ref[..., lo:hi].float().abs().max())
+        assert float(d.max()) <= 0.04 * scale
+        assert float(d.mean()) <= 0.002 * scale
