@@ -1105,6 +1105,18 @@ def profile_case(kind: str):
         mb.prefill()
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_pop()
+    elif kind == "gemm-down":
+        # the model's down projection onto the residual (in place, with the next norm's row
+        # statistics) at T=131072: 3 warm-up launches, then one
+        from butterfly_b200 import glue
+        g = torch.Generator(device=dev).manual_seed(0)
+        H, I = MODEL["hidden"], MODEL["inter"]
+        act = torch.randn(MODEL_T, I, device=dev, generator=g).bfloat16()
+        wd = (torch.randn(H, I, device=dev, generator=g) / I ** 0.5).bfloat16()
+        x2 = torch.randn(MODEL_T, H, device=dev, generator=g).bfloat16()
+        ss = torch.empty(MODEL_T, 4 * (H // 256), device=dev, dtype=torch.float32)
+        for _ in range(4):
+            glue.gemm_residual(act, wd, x2, out=x2, ss_out=ss)
     elif kind in ("gemm-swiglu", "gemm-qkv"):
         # the model's gate/up (or q/k/v) projection at T=131072: 3 warm-up launches, then one
         from butterfly_b200 import glue
@@ -1139,7 +1151,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the batched-decode leg")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-shard", action="store_true", help="skip the sequence-sharded 262k leg")
-    ap.add_argument("--profile-case", choices=["prefill", "decode", "prefill-trace", "model-prefill", "model-decode", "prefill-128k",
+    ap.add_argument("--profile-case", choices=["prefill", "decode", "prefill-trace", "model-prefill", "model-decode", "prefill-128k", "gemm-down",
                                                       "gemm-swiglu", "gemm-qkv"], default=None,
                     help="small case for ncu: warm-up, then the launches to capture")
     args = ap.parse_args()

@@ -191,9 +191,10 @@ def _fused_layer_forward(self, hidden_states: torch.Tensor, position_embeddings=
         y = glue.gate_sigmoid_mul(out.transpose(1, 2), qg[..., dh:])  # out storage is [B,T,hq,dh]
     else:
         y = gated
-    if fold:
+    if st.fold_norms:
         # o_proj + residual (writing the row statistics), gate/up with the post-attention norm
-        # folded in, down_proj accumulated in place (writing the next layer's statistics)
+        # folded in, down_proj accumulated in place (writing the next layer's statistics; a
+        # sequence shard's next layer, which keeps its input norm kernel, ignores them)
         rs2 = torch.empty((B * T, 4 * (H // 256)), device=x.device, dtype=torch.float32)
         x2 = glue.gemm_residual(y, src.o_proj.weight, x, ss_out=rs2)
         act = glue.gemm_swiglu(x2, st.folded("gu", self.post_attention_layernorm.weight, st.w_gu), st.inter,
