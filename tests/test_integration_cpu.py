@@ -69,3 +69,42 @@ def test_layout_cache_is_bounded():
     for T in (100, 200, 300, 200):
         lay._layout(T)
     assert list(lay._layouts) == [300, 200]
+
+
+def test_fused_layer_state_folds_norms_and_tracks_weight_loads():
+    """fuse_qwen_decoder_layers on CPU: the folded-norm weights are round(W * (1 + g)) and are
+    recomputed after an in-place weight load (version counters), not served stale."""
+    from butterfly_b200.integrations.qwen_fused import fuse_qwen_decoder_layers, unfuse_qwen_decoder_layers
+    m = _tiny()
+    m = m.to(torch.bfloat16)
+    qt.swap_qwen_attention_with_butterfly_cuda(m, qt.compressed_config())
+    assert fuse_qwen_decoder_layers(m) == [0, 1]
+    layer = m.model.layers[0]
+    st = layer._bna_fused
+    assert st.fold_norms  # hidden 256, head_dim 128, intermediate 256: every GEMM epilogue applies
+    g = layer.input_layernorm.weight
+    with torch.no_grad():
+        g.copy_(torch.randn_like(g) * 0.1)
+    f1 = st.folded("qkv", g, st.w_qkv)
+    assert torch.equal(f1, (st.w_qkv.float() * (1 + g.float())[None]).to(st.w_qkv.dtype))
+    assert st.folded("qkv", g, st.w_qkv) is f1  # cached
+    with torch.no_grad():  # a weight load into the module (a view of the merged buffer)
+        layer.self_attn.fallback.q_proj.weight.mul_(2)
+    f2 = st.folded("qkv", g, st.w_qkv)
+    assert f2 is not f1
+    assert torch.equal(f2, (st.w_qkv.float() * (1 + g.float())[None]).to(st.w_qkv.dtype))
+    with torch.no_grad():
+        g.zero_()
+    assert torch.equal(st.folded("qkv", g, st.w_qkv), st.w_qkv)  # (1 + 0) folds to the weights
+    assert unfuse_qwen_decoder_layers(m) == [0, 1]
+
+
+def test_row_statistics_reused_only_for_the_same_storage_and_version():
+    from butterfly_b200.integrations.qwen_fused import _row_stats
+    x = torch.randn(2, 3, 256).bfloat16()
+    ss = torch.zeros(6, 4)
+    x._bna_row_ss = (ss, x.data_ptr(), x._version)
+    assert _row_stats(x, 6) is ss
+    x.add_(1)  # modified in place after the statistics were written: recomputed (needs the GPU)
+    with pytest.raises(ValueError):
+        _row_stats(x, 6)
