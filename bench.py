@@ -358,7 +358,7 @@ def run_model(args, ws, rank, local, dev, peaks):
                                      "the attention kernel below",
                      "attention_kernel": att},
         "decode": decode,
-        "launches_per_step": 7 * MODEL["layers"] + 1,
+        "launches_per_step": 7 * MODEL["layers"] + 3,
     }
 
 
@@ -1192,9 +1192,11 @@ def main():
         "cpu_baseline": cpu,
         "e2e": m["e2e"],
         "gpu_launches": args.steps * m["launches_per_step"],
-        "gpu_launches_note": "our kernels per prefill: per layer input RMSNorm, q/k/v GEMM with q/k norm+RoPE, "
-                             "compressor, gated prefill kernel, cache hand-off append, residual+RMSNorm, gate/up "
-                             "GEMM with SwiGLU (7), plus the final norm; cuBLAS runs o_proj and down_proj",
+        "gpu_launches_note": "our kernels per prefill: per layer the q/k/v GEMM (input RMSNorm folded in, q/k "
+                             "norm+RoPE epilogue), compressor, gated prefill kernel, cache hand-off append, o_proj "
+                             "GEMM + residual, gate/up GEMM (post-attention RMSNorm folded in, SwiGLU epilogue), "
+                             "down GEMM + residual (7); plus the first layer's row statistics, the final norm and "
+                             "the lm_head GEMV; no cuBLAS kernel runs in the prefill (ncu launch list)",
         "timing": "CUDA events around the timed prefills; decode from CUDA-graph replays",
         "clocks": m["clocks"],
         "decode": m["decode"],
