@@ -20,19 +20,33 @@
 //    projection is rounded, the norm computes in fp32 and rounds, and each rotary product and
 //    the sum are rounded.
 //
-// Tiles: 128 rows of h x 256 rows of W (two 128-row TMA boxes: gate rows j0.. and up rows
-// I + j0.. for SwiGLU, rows n0.. and n0 + 128.. otherwise).  K advances in 64-element
-// (128-byte) blocks: per block TMA loads a 16 KB h tile and the two 16 KB W tiles into one
-// 4-stage ring; placed back to back, the W tiles form the 256-row K-major B operand.
-// Persistent CTAs (one per SM) walk the tiles with the output column tile innermost, so the
-// CTAs in flight share h rows through L2.
+// Three epilogues share one persistent tcgen05 GEMM; the third is the residual add of
+// o_proj / down_proj (out = round(round(acc) + res), optionally writing per-row partial sums
+// of squares for the next RMSNorm).  The SwiGLU and q/k/v forms can fold the RMSNorm before
+// them in: the A operand is then the un-normalised residual, W carries (1 + norm weight) in
+// its columns, and each accumulator row is scaled by rsqrt(mean(x^2) + eps) from those sums.
 //
-// Warp roles (320 threads):
-//   warp 0       TMA producer (one lane)
-//   warp 1       TMEM allocator + MMA issuer (converged warp, one elected lane issues);
-//                accumulators double-buffered in TMEM columns [0, 256) and [256, 512)
-//   warps 2..9   epilogue: warp w reads TMEM lane quarter w % 4 (32 rows) and one 128-column
-//                half of the accumulator; its stores overlap the next tile's MMAs
+// Tiles (default form, CTA pairs, cta_group::2): a cluster of two CTAs computes 256 rows of h
+// x 256 rows of W as one M = 256, N = 256 MMA per 16-wide k-step; CTA r stages h rows
+// m0 + 128 r and the r-th 128-row W box (gate rows j0.. / up rows I + j0.. for SwiGLU, rows
+// n0.. / n0 + 128.. otherwise) in a 6-stage ring of 32 KB stages, so each CTA's accumulator
+// holds its 128 rows x all 256 columns (both halves of 128 SwiGLU outputs).  The single-CTA
+// form (BNA_GEMM_CTA_PAIR=0, kept for comparison) stages 128 rows of h and both W boxes in a
+// 4-stage ring of 48 KB stages.  K advances in 64-element (128-byte) blocks.  Persistent CTAs
+// (one per SM) walk the tiles with the output column tile innermost, so the CTAs in flight
+// share h rows through L2.
+//
+// Warp roles:
+//   warp 0       TMA producer (one lane; in both CTAs of a pair, whose tiles all land on the
+//                leader's barrier)
+//   warp 1       TMEM allocator + MMA issuer (converged warp, one elected lane issues; in a
+//                pair only the leader issues, for both CTAs); accumulators double-buffered in
+//                TMEM columns [0, 256) and [256, 512)
+//   warps 2..    epilogue, 16 warps (8 for q/k/v): warp w reads TMEM lane quarter w % 4 (32
+//                rows) and its part of the columns; its stores overlap the next tile's MMAs
+// In a pair, the leader's commits arrive on both CTAs' barriers and both CTAs' epilogue warps
+// arrive on the leader's accumulator-empty barrier; a cluster barrier at the end keeps either
+// CTA from leaving while the other's MMAs, commits or arrivals may still reach it.
 // Every wait is bounded: a timeout sets the CTA abort flag and the device error word, the
 // roles wind down, in-flight copies and MMAs are drained (again with bounded waits) and the
 // TMEM is freed.
