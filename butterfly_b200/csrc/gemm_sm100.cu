@@ -1,15 +1,15 @@
 // gemm_sm100.cu — projections of the Qwen3.5 decoder layer on Blackwell tensor cores, with
 // the elementwise step that follows each one applied in the epilogue.
 //
-// Two epilogues share one persistent tcgen05 GEMM (out = h . W^T, fp32 accumulation):
+// Epilogues of one persistent tcgen05 GEMM (out = h . W^T, fp32 accumulation):
 //
 //  * SwiGLU (the MLP's gate/up projection, transformers' Qwen3_5MLP
 //    down_proj(act_fn(gate_proj(x)) * up_proj(x))):
 //        act[m, j] = silu(h[m,:] . Wg[j,:]) * (h[m,:] . Wu[j,:])     Wg = W[0:I], Wu = W[I:2I]
-//    A tile pairs 128 gate rows with the 128 matching up rows of W, so one M = 128, N = 256
-//    accumulator holds both halves of 128 output columns; the [M, 2I] gate/up product never
-//    reaches HBM.  The gate and up products, silu(gate) and the product are each rounded to
-//    the 16-bit type, as the eager ops.
+//    A tile pairs 128 gate rows with the 128 matching up rows of W, so one accumulator row
+//    holds both halves of 128 output columns; the [M, 2I] gate/up product never reaches HBM.
+//    The gate and up products, silu(gate) and the product are each rounded to the 16-bit
+//    type, as the eager ops (SiLU from the fast exponential and divide).
 //
 //  * q/k norm + RoPE (the attention's merged q/k/v projection; Qwen3_5Attention.forward and
 //    bna/integrations/qwen_torch.py:535-573: q_norm / k_norm per head, then the rotary
@@ -20,7 +20,7 @@
 //    projection is rounded, the norm computes in fp32 and rounds, and each rotary product and
 //    the sum are rounded.
 //
-// Three epilogues share one persistent tcgen05 GEMM; the third is the residual add of
+// The third epilogue is the residual add of
 // o_proj / down_proj (out = round(round(acc) + res), optionally writing per-row partial sums
 // of squares for the next RMSNorm).  The SwiGLU and q/k/v forms can fold the RMSNorm before
 // them in: the A operand is then the un-normalised residual, W carries (1 + norm weight) in
